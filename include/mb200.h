@@ -1,0 +1,140 @@
+/*
+ * libmb200 — the C ABI of the MetalBench B200 backend.
+ *
+ * This library replaces the reference's native host dispatcher
+ * (metal/scripts/main.mm:73-197, timing.mm:125-193, setup.cpp:116-136) and its
+ * Metal kernels. Python (the harness, via ctypes) or any FFI binds these
+ * symbols; no C++ types, exceptions or torch types cross the boundary.
+ *
+ * Conventions
+ *   - Every function returns 0 on success or a negative MB_ERR_* code; the
+ *     message of the last failure on the calling thread is mb_last_error().
+ *   - Device-pointer entry points (mb_<kernel>_*) take plain device pointers,
+ *     sizes and a cudaStream_t passed as void*; they only enqueue work.
+ *   - mb_run is the manifest-style entry point: host (or device) buffers by
+ *     reference binding index, timed warmup+iters launches, outputs copied back.
+ *   - Calls are serialised per device by the caller; one process per GPU.
+ */
+#ifndef MB200_H
+#define MB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MB_OK 0
+#define MB_ERR_BAD_ARG -1       /* wrong shape / size / alignment / dtype      */
+#define MB_ERR_UNKNOWN_KERNEL -2 /* name not in the kernel table               */
+#define MB_ERR_CUDA -3          /* a CUDA runtime/driver call failed           */
+#define MB_ERR_NCCL -4          /* an NCCL call failed                          */
+#define MB_ERR_TIMEOUT -5       /* a bounded device wait or comm init timed out */
+#define MB_ERR_NOT_INIT -6      /* mb_init was not called                       */
+
+/* ---- dtype tags (superset of mlx_helpers.py:83-89 "f32|f16|i32|u32") ---- */
+#define MB_F32 0
+#define MB_F16 1
+#define MB_I32 2
+#define MB_U32 3
+#define MB_BF16 4
+
+/* ---- buffer roles (manifest "role", mlx_helpers.py:301-313) ------------- */
+#define MB_ROLE_INPUT 0
+#define MB_ROLE_OUTPUT 1
+
+/* ---- buffer flags -------------------------------------------------------- */
+#define MB_DEVICE_PTR 1 /* ptr is already a device pointer (e.g. a torch tensor) */
+
+typedef struct mb_buf {
+  int binding; /* reference [[buffer(i)]] index                               */
+  int role;    /* MB_ROLE_INPUT / MB_ROLE_OUTPUT                              */
+  int dtype;   /* MB_F32 ...                                                  */
+  int flags;   /* MB_DEVICE_PTR                                               */
+  void* ptr;   /* host pointer (inputs read, outputs written) or device ptr  */
+  size_t bytes;
+} mb_buf;
+
+typedef struct mb_scalar {
+  int binding; /* reference scalar binding index (registry "scalars")         */
+  int dtype;   /* MB_U32 / MB_I32 / MB_F32                                    */
+  union {
+    uint32_t u;
+    int32_t i;
+    float f;
+  } v;
+} mb_scalar;
+
+/* Timing of mb_run, same statistics as timing.mm:150-159: per-launch device
+ * times sorted, median = times[n/2]. */
+typedef struct mb_timing {
+  double min_ms;
+  double median_ms;
+  double mean_ms;
+  int iters;
+  int smem_bytes;      /* dynamic shared memory per CTA of the main kernel    */
+  int threads_per_cta; /* threads per CTA of the main kernel                  */
+  int launches_per_iter;
+  double h2d_ms; /* host->device copy time of the inputs (0 for device ptrs) */
+  double d2h_ms; /* device->host copy time of the outputs                    */
+} mb_timing;
+
+/* Device description (replaces setup.cpp:116-136 chip detection). */
+typedef struct mb_device {
+  char name[128];
+  char type[32];   /* "b200" on B200, else "sm<major><minor>"                 */
+  char bucket[32]; /* results/<bucket>/ directory key                         */
+  int sm_count;
+  int cc_major;
+  int cc_minor;
+  int cpu_cores;
+  uint64_t hbm_bytes;
+  uint64_t ram_bytes;
+  int l2_bytes;
+  int smem_per_block_optin;
+} mb_device;
+
+/* ---- lifecycle / manifest API (SURVEY boundary: main.mm replacement) ---- */
+
+/* Select the device for this process. rank/world/nccl_id_path are used by the
+ * tensor-parallel entry points (world > 1); pass 0/1/NULL for one GPU.
+ * timeout_ms bounds communicator set-up. */
+int mb_init(int device, int rank, int world, const char* nccl_id_path, int timeout_ms);
+void mb_shutdown(void);
+const char* mb_last_error(void);
+int mb_device_info(mb_device* out);
+
+/* Names understood by mb_run, comma separated (static storage). */
+const char* mb_kernel_names(void);
+
+/* Run `kernel` warmup+iters times on the bound buffers and report per-launch
+ * device time (main.mm:161-165 + timing.mm:125-193). config_json is an optional
+ * flat JSON object of extra keys (e.g. {"padding":1,"flush_l2":true}). */
+int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const mb_scalar* scalars, int nsc,
+           const char* config_json, int warmup, int iters, mb_timing* out);
+
+/* Status word that bounded device waits write on timeout; 0 = clean. Reading
+ * it synchronises the device. mb_clear_device_status resets it. */
+int mb_device_status(uint32_t* out);
+int mb_clear_device_status(void);
+
+/* ---- transpose_2d (metal/kernels/common/transpose_2d/default.metal:10-48;
+ *      hook mlx/kernels/common/transpose_2d.py:10-11) -------------------- */
+
+/* out[c][r] = in[r][c] for an fp32 rows x cols row-major matrix. */
+int mb_transpose_2d_f32(const float* in, float* out, int64_t rows, int64_t cols, void* stream);
+
+/* out[b][c][r] = in[b][r][c] for bf16 (raw uint16) tensors [batch, rows, cols]. */
+int mb_transpose_batched_bf16(const uint16_t* in, uint16_t* out, int64_t batch, int64_t rows,
+                              int64_t cols, void* stream);
+
+/* Same for fp32 tensors [batch, rows, cols]. */
+int mb_transpose_batched_f32(const float* in, float* out, int64_t batch, int64_t rows,
+                             int64_t cols, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MB200_H */

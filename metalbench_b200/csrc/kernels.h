@@ -1,0 +1,62 @@
+// Internal (non-ABI) registry of the kernels mb_run can dispatch by name.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/mb200.h"
+
+namespace mb {
+
+struct Config {
+  std::map<std::string, std::string> kv;
+  double num(const char* k, double dflt) const;
+  std::string str(const char* k, const char* dflt) const;
+};
+Config parse_config(const char* js);
+
+struct RunArgs {
+  struct Buf {
+    int binding, role, dtype;
+    size_t bytes;
+    void* host;  // caller pointer
+    void* dev;   // device pointer bound to the kernel
+  };
+  std::vector<Buf> bufs;
+  std::vector<mb_scalar> scalars;
+  Config config;
+  const Buf* buf(int binding) const;
+  bool scalar(int binding, double* out) const;
+};
+
+// What prepare() leaves behind: the per-iteration launch, an optional
+// post-timing step, scratch allocations (freed on destruction) and the launch
+// shape reported in mb_timing.
+struct KernelState {
+  std::function<int(cudaStream_t)> launch;
+  std::function<int(cudaStream_t)> finish;
+  std::vector<void*> scratch;
+  std::vector<std::function<void()>> cleanup;
+  int smem_bytes = 0, threads_per_cta = 0, launches_per_iter = 1;
+  ~KernelState() {
+    for (auto& f : cleanup) f();
+    for (void* p : scratch) cudaFree(p);
+  }
+};
+
+struct KernelEntry {
+  std::string name;
+  std::function<int(const RunArgs&, KernelState&, cudaStream_t)> prepare;
+};
+
+void register_kernel(const KernelEntry& e);
+void register_all_kernels();  // defined in registry.cu
+
+// tensor parallel communicator (tp.cu)
+int tp_init(int rank, int world, const char* nccl_id_path, int timeout_ms);
+void tp_shutdown();
+
+}  // namespace mb

@@ -1,0 +1,93 @@
+// Kernel table behind mb_run: binds reference binding indices and scalars to
+// the device-pointer entry points. Binding numbers follow the reference
+// registry entries (mlx/kernels/common/registry.py, mlx/kernels/full/registry.py).
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mb {
+namespace {
+
+int need_buf(const RunArgs& a, int binding, int role, const RunArgs::Buf** out) {
+  const RunArgs::Buf* b = a.buf(binding);
+  MB_REQUIRE(b != nullptr, "binding %d missing", binding);
+  MB_REQUIRE(b->role == role, "binding %d has role %d, expected %d", binding, b->role, role);
+  *out = b;
+  return MB_OK;
+}
+
+int need_scalar(const RunArgs& a, int binding, int64_t* out) {
+  double v = 0;
+  MB_REQUIRE(a.scalar(binding, &v), "scalar binding %d missing", binding);
+  *out = (int64_t)v;
+  return MB_OK;
+}
+
+#define TRY(x)          \
+  do {                  \
+    int _rc = (x);      \
+    if (_rc) return _rc; \
+  } while (0)
+
+// transpose_2d: registry common/registry.py:165-179 — in@0, out@1, rows@2, cols@3.
+int prep_transpose_2d(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *in, *out;
+  int64_t rows, cols;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &in));
+  TRY(need_buf(a, 1, MB_ROLE_OUTPUT, &out));
+  TRY(need_scalar(a, 2, &rows));
+  TRY(need_scalar(a, 3, &cols));
+  const int esz = in->dtype == MB_BF16 ? 2 : 4;
+  MB_REQUIRE(in->dtype == MB_F32 || in->dtype == MB_BF16, "transpose_2d: dtype must be f32 or bf16");
+  MB_REQUIRE(in->bytes == (size_t)(rows * cols * esz) && out->bytes == in->bytes,
+             "transpose_2d: buffer sizes do not match %lldx%lld", (long long)rows, (long long)cols);
+  void* ip = in->dev;
+  void* op = out->dev;
+  const int dt = in->dtype;
+  st.threads_per_cta = 256;
+  st.smem_bytes = dt == MB_BF16 ? 16640 : 16384;
+  st.launch = [=](cudaStream_t s) {
+    return dt == MB_BF16 ? mb_transpose_batched_bf16((const uint16_t*)ip, (uint16_t*)op, 1, rows, cols, s)
+                         : mb_transpose_2d_f32((const float*)ip, (float*)op, rows, cols, s);
+  };
+  return MB_OK;
+}
+
+// transpose_batched: in@0 [batch, rows, cols], out@1, batch@2, rows@3, cols@4.
+int prep_transpose_batched(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *in, *out;
+  int64_t batch, rows, cols;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &in));
+  TRY(need_buf(a, 1, MB_ROLE_OUTPUT, &out));
+  TRY(need_scalar(a, 2, &batch));
+  TRY(need_scalar(a, 3, &rows));
+  TRY(need_scalar(a, 4, &cols));
+  MB_REQUIRE(in->dtype == MB_F32 || in->dtype == MB_BF16, "transpose_batched: dtype must be f32 or bf16");
+  const int esz = in->dtype == MB_BF16 ? 2 : 4;
+  MB_REQUIRE(in->bytes == (size_t)(batch * rows * cols * esz) && out->bytes == in->bytes,
+             "transpose_batched: buffer sizes do not match");
+  void* ip = in->dev;
+  void* op = out->dev;
+  const int dt = in->dtype;
+  st.threads_per_cta = 256;
+  st.smem_bytes = dt == MB_BF16 ? 16640 : 16384;
+  st.launch = [=](cudaStream_t s) {
+    return dt == MB_BF16
+               ? mb_transpose_batched_bf16((const uint16_t*)ip, (uint16_t*)op, batch, rows, cols, s)
+               : mb_transpose_batched_f32((const float*)ip, (float*)op, batch, rows, cols, s);
+  };
+  return MB_OK;
+}
+
+}  // namespace
+
+void register_all_kernels() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    register_kernel({"transpose_2d", prep_transpose_2d});
+    register_kernel({"transpose_batched", prep_transpose_batched});
+  });
+}
+
+}  // namespace mb

@@ -1,0 +1,70 @@
+"""Torch-tensor front end of libmb200 (device memory and streams come from torch).
+
+Each function validates its tensors, then calls the C-ABI entry point with raw
+device pointers on torch's current stream. There is no fallback: a missing
+library or a non-CUDA tensor raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_inited: set[int] = set()
+
+
+def init(device: int | None = None) -> None:
+    """mb_init for one GPU (idempotent per device)."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    if dev not in _inited:
+        _lib.call("mb_init", dev, 0, 1, None, 0)
+        _inited.add(dev)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cuda(t: torch.Tensor, name: str, dtypes) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name}: expected a CUDA tensor (no CPU fallback)")
+    if t.dtype not in dtypes:
+        raise TypeError(f"{name}: dtype {t.dtype} not in {dtypes}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous tensor")
+
+
+def transpose_2d(a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = a.T for a 2-D fp32 or bf16 tensor (bit-exact data movement)."""
+    _cuda(a, "transpose_2d", (torch.float32, torch.bfloat16))
+    if a.dim() != 2:
+        raise ValueError("transpose_2d: expected a 2-D tensor")
+    init(a.device.index)
+    R, Cc = a.shape
+    if out is None:
+        out = torch.empty((Cc, R), dtype=a.dtype, device=a.device)
+    _cuda(out, "transpose_2d(out)", (a.dtype,))
+    if tuple(out.shape) != (Cc, R):
+        raise ValueError("transpose_2d: out has the wrong shape")
+    if a.dtype == torch.float32:
+        _lib.call("mb_transpose_2d_f32", a.data_ptr(), out.data_ptr(), R, Cc, _stream())
+    else:
+        _lib.call("mb_transpose_batched_bf16", a.data_ptr(), out.data_ptr(), 1, R, Cc, _stream())
+    return out
+
+
+def transpose_batched(a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Swap the last two axes of a [batch, rows, cols] fp32 or bf16 tensor."""
+    _cuda(a, "transpose_batched", (torch.float32, torch.bfloat16))
+    if a.dim() != 3:
+        raise ValueError("transpose_batched: expected a 3-D tensor")
+    init(a.device.index)
+    Bn, R, Cc = a.shape
+    if out is None:
+        out = torch.empty((Bn, Cc, R), dtype=a.dtype, device=a.device)
+    _cuda(out, "transpose_batched(out)", (a.dtype,))
+    if tuple(out.shape) != (Bn, Cc, R):
+        raise ValueError("transpose_batched: out has the wrong shape")
+    fn = "mb_transpose_batched_f32" if a.dtype == torch.float32 else "mb_transpose_batched_bf16"
+    _lib.call(fn, a.data_ptr(), out.data_ptr(), Bn, R, Cc, _stream())
+    return out

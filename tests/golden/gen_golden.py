@@ -1,0 +1,77 @@
+"""Generate golden fixtures by executing the REFERENCE's own hook files.
+
+Run in the build container (where the read-only reference checkout exists):
+
+    python tests/golden/gen_golden.py [--reference PATH]
+
+MLX is not installed here, so ``oracle/mlx_shim`` (a numpy implementation of
+the MLX ops the hooks use) is put on ``sys.path`` as ``mlx``. The script then
+loads each hook (``mlx/kernels/<set>/<name>.py``) from the reference checkout,
+builds its ``Model`` exactly as the reference harness does
+(mlx/scripts/mlx_helpers.py:219-257: ``Model()`` with default arguments and one
+N(0,1) float32 input per registry input shape) and stores inputs and outputs
+in ``tests/golden/<name>.npz``. The fixtures are what pins ``oracle.ops``;
+nothing at test time reads the reference checkout.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import importlib.util
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+
+# (name, set, registry input shapes, seed). Shapes are the reference registry
+# shapes (common/registry.py:129,165-179,469-477; full/registry.py:87-104),
+# shrunk where the reference shape would make the fixture large.
+CASES = [
+    ("sqr_mm", "common", [(64, 64), (64, 64)], 0),
+    ("transpose_2d", "common", [(48, 80)], 1),
+    ("conv2d", "common", [(2, 10, 12, 64), (128, 3, 3, 64)], 2),
+    ("llama_decoder_layer", "full",
+     [(64, 128), (128, 128 + 2 * 2 * 32), (128, 128), (128, 2 * 256), (256, 128)], 3),
+]
+
+
+def _load_hook(ref: Path, kset: str, name: str):
+    path = ref / "mlx" / "kernels" / kset / f"{name}.py"
+    spec = importlib.util.spec_from_file_location(f"_ref_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod, hashlib.sha256(path.read_bytes()).hexdigest()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=str(Path("/", "root", "reference")))
+    args = ap.parse_args(argv)
+    ref = Path(args.reference)
+    try:
+        import mlx.core  # noqa: F401
+        print("[golden] using real mlx", file=sys.stderr)
+    except ImportError:
+        sys.path.insert(0, str(REPO / "oracle" / "mlx_shim"))
+        print("[golden] mlx absent: using oracle/mlx_shim", file=sys.stderr)
+    import mlx.core as mx
+
+    for name, kset, shapes, seed in CASES:
+        mod, digest = _load_hook(ref, kset, name)
+        rng = np.random.default_rng(seed)
+        inputs = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+        model = mod.Model()
+        out = np.asarray(model.forward(*[mx.array(x) for x in inputs]), dtype=np.float32)
+        blob = {f"in{i}": x for i, x in enumerate(inputs)}
+        blob["out"] = out
+        blob["hook_sha256"] = np.array(digest)
+        blob["seed"] = np.array(seed)
+        np.savez_compressed(HERE / f"{name}.npz", **blob)
+        print(f"[golden] {name}: inputs {shapes} -> out {out.shape}", file=sys.stderr)
+
+
+if __name__ == "__main__":
+    main()
