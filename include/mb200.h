@@ -134,6 +134,24 @@ int mb_transpose_batched_bf16(const uint16_t* in, uint16_t* out, int64_t batch, 
 int mb_transpose_batched_f32(const float* in, float* out, int64_t batch, int64_t rows,
                              int64_t cols, void* stream);
 
+/* ---- GEMM on the tcgen05 core (registry helper matmul,
+ *      mlx/kernels/common/registry.py:44-61; sqr_mm hook
+ *      mlx/kernels/common/sqr_mm.py:10-11; Metal kernel
+ *      metal/kernels/common/sqr_mm.metal:19-111) ------------------------- */
+
+/* C[M,N] (bf16) = A[M,K] (bf16, row-major) @ B, fp32 accumulation.
+ * b_layout 0: B is [N,K] row-major (K contiguous, "weights" layout);
+ * b_layout 1: B is [K,N] row-major (the reference's A @ B layout).
+ * Needs K % 8 == 0, N % 8 == 0, 16-byte aligned pointers. */
+int mb_gemm_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N,
+                 int64_t K, int b_layout, void* stream);
+
+/* C[M,N] (fp32) = A[M,K] @ B[K,N], all fp32 row-major, fp32-accurate via
+ * 3xTF32 on the tensor cores (hi*hi + hi*lo + lo*hi, fp32 accumulate).
+ * Needs K % 4 == 0, N % 4 == 0, 16-byte aligned pointers. */
+int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

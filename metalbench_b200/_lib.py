@@ -64,6 +64,8 @@ SIGNATURES = {
     "mb_transpose_2d_f32": (C.c_int, [_P, _P, _I64, _I64, _P]),
     "mb_transpose_batched_bf16": (C.c_int, [_P, _P, _I64, _I64, _I64, _P]),
     "mb_transpose_batched_f32": (C.c_int, [_P, _P, _I64, _I64, _I64, _P]),
+    "mb_gemm_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "mb_sqr_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P]),
 }
 
 _lib = None

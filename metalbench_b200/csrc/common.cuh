@@ -48,10 +48,6 @@ int num_sms();
 #define MB_DEV_TIMEOUT_MMA 0x2u
 #define MB_DEV_TIMEOUT_EPI 0x4u
 
-// ~2^28 polls of try_wait (each try_wait itself suspends for a hardware time
-// slice) is well over a second on B200; a correct pipeline never gets close.
-#define MB_SPIN_LIMIT (1u << 28)
-
 namespace mbd {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -92,14 +88,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records `code` in *status) if the phase
-// never completes. Callers then stop issuing work and fall through to teardown.
+// Bounded waits give up after MB_WAIT_NS of wall time on the SM's global
+// timer (2 s; a correct pipeline waits microseconds), record a status code and
+// let the caller fall through to teardown instead of hanging the GPU.
+#define MB_WAIT_NS 2000000000ull
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: returns false (and records `code` in *status, and raises the
+// CTA-wide *abort flag when given) if the phase never completes or another
+// role of the CTA already gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
-                                          uint32_t code) {
-  for (uint32_t i = 0; i < MB_SPIN_LIMIT; ++i) {
+                                          uint32_t code, volatile int* abort_flag = nullptr) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (abort_flag && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > MB_WAIT_NS) break;
+    }
   }
   if (status) atomicOr(status, code);
+  if (abort_flag) *abort_flag = 1;
   return false;
 }
 

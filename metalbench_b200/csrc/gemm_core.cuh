@@ -1,0 +1,325 @@
+// Persistent, warp-specialised tcgen05 GEMM core for sm_100a.
+//
+//   D[M, N] = sum_k A[m, k] * B[n, k]       (A: M x K, K contiguous)
+//   B is either K-major ([N, K], K contiguous) or MN-major ([K, N], N contiguous).
+//
+// One CTA per SM walks a static list of output tiles (BM = 128 rows x BN
+// columns, optionally split along K). Roles inside the CTA:
+//   warp 0      TMA producer: fills a STAGES-deep ring of 128-byte-swizzled
+//               A/B tiles (64 bf16 or 32 fp32 of K per stage).
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma into one of
+//               two TMEM accumulators (128 lanes x BN fp32 columns each) and
+//               frees ring slots with tcgen05.commit.
+//   warp 2      allocates / frees TMEM.
+//   warps 4-7   epilogue: tcgen05.ld the finished accumulator (warp w owns
+//               TMEM lanes 32*(w%4)..+31 = tile rows), apply the fused
+//               epilogue functor, store; then hand the accumulator back.
+//   warps 8-11  (TF32x3 mode only) split every fp32 tile in shared memory into
+//               a tf32 "hi" part (low 13 mantissa bits cleared) and the exact
+//               remainder "lo", so the MMA warp can issue hi*hi + hi*lo + lo*hi.
+// With two accumulators the epilogue of tile i overlaps the main loop of
+// tile i+1. Every mbarrier wait is bounded (common.cuh) and reports through
+// the device status word instead of hanging.
+#pragma once
+#include "common.cuh"
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int KBYTES = 128;  // K extent of one stage in bytes (one swizzle row)
+
+enum class Mode { BF16 = 0, TF32X3 = 1 };
+
+__host__ __device__ constexpr int elem_bytes(Mode m) { return m == Mode::BF16 ? 2 : 4; }
+__host__ __device__ constexpr int num_warps(Mode m) { return m == Mode::TF32X3 ? 12 : 8; }
+
+template <Mode MODE, int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * KBYTES;
+  static constexpr int B_BYTES = BN * KBYTES;
+  static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;  // raw/hi (+ lo)
+  static constexpr int STAGE_BYTES = PARTS * (A_BYTES + B_BYTES);
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  // barriers: full, ready (after split), empty per stage; tfull, tempty x2
+  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
+  static constexpr int TOTAL = 1024 /*alignment slack*/ + RING_BYTES + BAR_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+};
+
+// Static tile list, rasterised in groups of GROUP_M tile-rows so that CTAs
+// running at the same time share A panels and B panels in L2.
+struct Sched {
+  int tiles_m, tiles_n, ksplit, kblocks, kb_per_split;
+  static constexpr int GROUP_M = 16;
+  __host__ __device__ int total() const { return tiles_m * tiles_n * ksplit; }
+  __device__ void get(int t, int& tm, int& tn, int& ks) const {
+    ks = t % ksplit;
+    t /= ksplit;
+    const int per_group = GROUP_M * tiles_n;
+    const int g = t / per_group;
+    const int first = g * GROUP_M;
+    const int gsize = min(tiles_m - first, GROUP_M);
+    const int r = t % per_group;
+    tm = first + r % gsize;
+    tn = r / gsize;
+  }
+  __device__ void krange(int ks, int& kb0, int& kb1) const {
+    kb0 = ks * kb_per_split;
+    kb1 = min(kblocks, kb0 + kb_per_split);
+  }
+};
+
+// Epilogue context handed to the functor for one tile: the TMEM address of
+// this thread's row (lane) at column 0 of the accumulator, the global row,
+// the first global column, the split index and whether the row is in range.
+struct EpiCtx {
+  uint32_t taddr;
+  int row;
+  int n0;
+  int ks;
+  bool row_ok;
+};
+
+
+// ---------------------------------------------------------------------------
+// TMA producer for plain GEMM operands (2-D tensor maps, 128-byte swizzle).
+//   A map: inner K, outer M, box {128 B of K, 128 rows}.
+//   B K-major map: inner K, outer N, box {128 B of K, BN rows}.
+//   B MN-major map: inner N, outer K, box {128 B of N, K rows of one stage};
+//   BN / (128 B of N) boxes side by side (LBO apart) make one B stage.
+// ---------------------------------------------------------------------------
+template <Mode MODE, int BN, bool B_MN>
+struct GemmProducer {
+  CUtensorMap a, b;
+  static constexpr int KE = KBYTES / elem_bytes(MODE);  // K elements per stage
+  static constexpr uint32_t BYTES = (BM + BN) * KBYTES;
+  static constexpr int B_BOX_BYTES = KE * KBYTES;       // one MN-major box
+  __device__ void prefetch() const {
+    mbd::prefetch_tmap(&a);
+    mbd::prefetch_tmap(&b);
+  }
+  __device__ void load(uint8_t* sA, uint8_t* sB, uint64_t* bar, int tm, int tn, int kb) const {
+    mbd::tma_load_2d(sA, &a, bar, kb * KE, tm * BM);
+    if constexpr (!B_MN) {
+      mbd::tma_load_2d(sB, &b, bar, kb * KE, tn * BN);
+    } else {
+#pragma unroll
+      for (int j = 0; j < BN / KE; ++j)
+        mbd::tma_load_2d(sB + j * B_BOX_BYTES, &b, bar, tn * BN + j * KE, kb * KE);
+    }
+  }
+  // Shared-memory descriptors for MMA k-step kk of a stage.
+  static constexpr int KSTEPS = 4;  // 16 bf16 or 8 tf32 per MMA = 32 bytes of K
+  __device__ static uint64_t a_desc(uint32_t sA, int kk) {
+    return mbd::sw128_desc(sA + kk * 32, 16, 1024);
+  }
+  __device__ static uint64_t b_desc(uint32_t sB, int kk) {
+    if constexpr (!B_MN) return mbd::sw128_desc(sB + kk * 32, 16, 1024);
+    // MN-major: one k-step is 16 bf16 = two 8-row groups, or 8 tf32 = one.
+    constexpr int step = MODE == Mode::BF16 ? 2048 : 1024;
+    return mbd::sw128_desc(sB + kk * step, B_BOX_BYTES, 1024);
+  }
+};
+
+template <Mode MODE, int BN, int STAGES, bool B_MN, class Producer, class Epi>
+__global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
+    gemm_kernel(const __grid_constant__ Producer prod, const __grid_constant__ Epi epi,
+                const Sched sched, uint32_t* status) {
+  using S = Smem<MODE, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + S::RING_BYTES);
+  uint64_t* ready = full + STAGES;
+  uint64_t* empty = ready + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* drain = reinterpret_cast<uint64_t*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto sA = [&](int s) { return base + s * S::STAGE_BYTES; };
+  auto sB = [&](int s) { return base + s * S::STAGE_BYTES + S::A_BYTES; };
+  // TF32x3: the "lo" halves follow the raw/hi halves of the stage.
+  auto sAlo = [&](int s) { return base + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
+  auto sBlo = [&](int s) { return base + s * S::STAGE_BYTES + 2 * S::A_BYTES + S::B_BYTES; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbd::mbar_init(&full[s], 1);
+      mbd::mbar_init(&ready[s], 128);
+      mbd::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbd::mbar_init(&tfull[b], 1);
+      mbd::mbar_init(&tempty[b], 128);
+    }
+    mbd::mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbd::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) prod.prefetch();
+  if (warp == 2) mbd::tmem_alloc(tmem_slot, S::TMEM_COLS);
+  __syncthreads();
+  mbd::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = sched.total();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;  // bit s: parity of the last load issued into stage s
+      uint32_t used = 0;    // bit s: stage s received at least one load
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        int tm, tn, ks, kb0, kb1;
+        sched.get(t, tm, tn, ks);
+        sched.krange(ks, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbd::mbar_wait(&empty[stage], phase ^ 1, status, MB_DEV_TIMEOUT_TMA, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbd::mbar_expect_tx(&full[stage], Producer::BYTES);
+          prod.load(sA(stage), sB(stage), &full[stage], tm, tn, kb);
+          issued = (issued & ~(1u << stage)) | (phase << stage);
+          used |= 1u << stage;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Never leave a bulk copy in flight into shared memory we are about to
+      // release: wait (bounded) for the last load of every stage.
+      for (int s = 0; s < STAGES; ++s)
+        if (used & (1u << s)) mbd::mbar_wait(&full[s], (issued >> s) & 1, status, MB_DEV_TIMEOUT_TMA);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t fmt = MODE == Mode::BF16 ? 1u : 2u;
+      constexpr uint32_t idesc = mbd::make_idesc(fmt, BM, BN, 0, B_MN ? 1u : 0u);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++i) {
+        int tm, tn, ks, kb0, kb1;
+        sched.get(t, tm, tn, ks);
+        sched.krange(ks, kb0, kb1);
+        const int buf = i & 1;
+        const uint32_t tph = (i >> 1) & 1;
+        if (!mbd::mbar_wait(&tempty[buf], tph ^ 1, status, MB_DEV_TIMEOUT_MMA, abort_flag)) break;
+        mbd::tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          uint64_t* gate = MODE == Mode::TF32X3 ? &ready[stage] : &full[stage];
+          if (!mbd::mbar_wait(gate, phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbd::tc_fence_after();
+          const uint32_t a0 = mbd::smem_u32(sA(stage)), b0 = mbd::smem_u32(sB(stage));
+#pragma unroll
+          for (int kk = 0; kk < Producer::KSTEPS; ++kk) {
+            const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
+            const uint64_t ad = Producer::a_desc(a0, kk), bd = Producer::b_desc(b0, kk);
+            if constexpr (MODE == Mode::BF16) {
+              mbd::mma_f16(d, ad, bd, idesc, acc);
+            } else {
+              const uint64_t adl = Producer::a_desc(mbd::smem_u32(sAlo(stage)), kk);
+              const uint64_t bdl = Producer::b_desc(mbd::smem_u32(sBlo(stage)), kk);
+              mbd::mma_tf32(d, adl, bd, idesc, acc);  // lo * hi
+              mbd::mma_tf32(d, ad, bdl, idesc, 1u);   // hi * lo
+              mbd::mma_tf32(d, ad, bd, idesc, 1u);    // hi * hi
+            }
+          }
+          mbd::mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mbd::mma_commit(&tfull[buf]);
+      }
+      // All MMAs issued by this thread are complete before TMEM is freed.
+      mbd::mma_commit(drain);
+      mbd::mbar_wait(drain, 0, status, MB_DEV_TIMEOUT_MMA);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      int tm, tn, ks;
+      sched.get(t, tm, tn, ks);
+      const int buf = i & 1;
+      const uint32_t tph = (i >> 1) & 1;
+      if (!mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag)) break;
+      mbd::tc_fence_after();
+      EpiCtx c;
+      c.taddr = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
+      c.row = tm * BM + q * 32 + lane;
+      c.n0 = tn * BN;
+      c.ks = ks;
+      c.row_ok = c.row < epi.M;
+      epi(c);
+      mbd::tc_fence_before();
+      mbd::mbar_arrive(&tempty[buf]);
+    }
+  } else if (MODE == Mode::TF32X3 && warp >= 8) {
+    // ---------------- fp32 -> tf32 hi + lo splitter ----------------
+    const int ct = threadIdx.x - 256;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      int tm, tn, ks, kb0, kb1;
+      sched.get(t, tm, tn, ks);
+      sched.krange(ks, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // A (hi in place, lo behind B) then B: position-preserving, so the
+        // swizzle of the tile does not matter.
+        uint4* ra = reinterpret_cast<uint4*>(sA(stage));
+        uint4* la = reinterpret_cast<uint4*>(sAlo(stage));
+        constexpr int NA = S::A_BYTES / 16, NB = S::B_BYTES / 16;
+        for (int v = ct; v < NA + NB; v += 128) {
+          uint4* r = v < NA ? ra + v : reinterpret_cast<uint4*>(sB(stage)) + (v - NA);
+          uint4* l = v < NA ? la + v : reinterpret_cast<uint4*>(sBlo(stage)) + (v - NA);
+          uint4 x = *r, hi, lo;
+          hi.x = x.x & 0xFFFFE000u;
+          hi.y = x.y & 0xFFFFE000u;
+          hi.z = x.z & 0xFFFFE000u;
+          hi.w = x.w & 0xFFFFE000u;
+          lo.x = __float_as_uint(__uint_as_float(x.x) - __uint_as_float(hi.x));
+          lo.y = __float_as_uint(__uint_as_float(x.y) - __uint_as_float(hi.y));
+          lo.z = __float_as_uint(__uint_as_float(x.z) - __uint_as_float(hi.z));
+          lo.w = __float_as_uint(__uint_as_float(x.w) - __uint_as_float(hi.w));
+          *r = hi;
+          *l = lo;
+        }
+        mbd::fence_proxy_async();  // generic-proxy writes -> visible to tcgen05
+        mbd::mbar_arrive(&ready[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    mbd::tc_fence_after();
+    mbd::tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+}  // namespace gemm

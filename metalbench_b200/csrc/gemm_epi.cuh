@@ -1,0 +1,120 @@
+// Epilogue functors for the tcgen05 GEMM core. Each runs in the four
+// epilogue warps; thread (warp w, lane l) owns accumulator row 32*(w%4)+l and
+// reads it from TMEM 32 columns at a time. tcgen05.ld is warp-collective, so
+// every lane issues the loads and only the stores are predicated.
+#pragma once
+#include "gemm_core.cuh"
+
+namespace gemm {
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[16], s[16];
+  mbd::tmem_ld16(taddr, r);
+  mbd::tmem_ld16(taddr + 16, s);
+  mbd::tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    v[j] = __uint_as_float(r[j]);
+    v[16 + j] = __uint_as_float(s[j]);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // .x = a (low half)
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
+  return __uint_as_float(((uint32_t)b) << 16);
+}
+
+// Store 32 consecutive values of one row: vectorised when fully in range.
+__device__ __forceinline__ void store_row32(void* out, int64_t ldo, int out_f32, int row, int n,
+                                            int N, const float (&v)[32]) {
+  if (out_f32) {
+    float* p = reinterpret_cast<float*>(out) + (int64_t)row * ldo + n;
+    if (n + 32 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(p + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < N) p[j] = v[j];
+    }
+  } else {
+    uint16_t* p = reinterpret_cast<uint16_t*>(out) + (int64_t)row * ldo + n;
+    if (n + 32 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        w.x = pack_bf16(v[j], v[j + 1]);
+        w.y = pack_bf16(v[j + 2], v[j + 3]);
+        w.z = pack_bf16(v[j + 4], v[j + 5]);
+        w.w = pack_bf16(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(p + j) = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < N) {
+          __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+          p[j] = *reinterpret_cast<uint16_t*>(&h);
+        }
+    }
+  }
+}
+
+// out[row, n] = alpha * row_scale[row] * acc[row, n] (+ residual[row, n]),
+// stored as bf16 or fp32. row_scale and residual are optional (null).
+struct EpiStore {
+  int M, N;
+  void* out;
+  int64_t ldo;
+  int out_f32;
+  float alpha;
+  const float* row_scale;
+  const uint16_t* residual;  // bf16 [M, ld_res]
+  int64_t ld_res;
+  template <int BN>
+  __device__ void run(const EpiCtx& c) const {
+    const float sc = (c.row_ok && row_scale) ? row_scale[c.row] * alpha : alpha;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld32(c.taddr + c0, v);
+      const int n = c.n0 + c0;
+      if (!c.row_ok || n >= N) continue;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= sc;
+      if (residual) {
+        const uint16_t* r = residual + (int64_t)c.row * ld_res + n;
+        if (n + 32 <= N && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            const uint4 w = *reinterpret_cast<const uint4*>(r + j);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              v[j + 2 * m] += __uint_as_float(ws[m] << 16);
+              v[j + 2 * m + 1] += __uint_as_float(ws[m] & 0xFFFF0000u);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < N) v[j] += bf16_bits_to_f32(r[j]);
+        }
+      }
+      store_row32(out, ldo, out_f32, c.row, n, N, v);
+    }
+  }
+};
+
+// Adapter: the kernel calls epi(ctx); BN is fixed per instantiation.
+template <int BN, class E>
+struct Epi : E {
+  __device__ void operator()(const EpiCtx& c) const { E::template run<BN>(c); }
+};
+
+}  // namespace gemm

@@ -80,6 +80,55 @@ int prep_transpose_batched(const RunArgs& a, KernelState& st, cudaStream_t) {
   return MB_OK;
 }
 
+// sqr_mm: registry matmul helper common/registry.py:44-61 — A@0, B@1, C@2,
+// M@3, N@4, K@5, fp32 row-major.
+int prep_sqr_mm(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *A, *B, *Cb;
+  int64_t M, N, K;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &A));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &B));
+  TRY(need_buf(a, 2, MB_ROLE_OUTPUT, &Cb));
+  TRY(need_scalar(a, 3, &M));
+  TRY(need_scalar(a, 4, &N));
+  TRY(need_scalar(a, 5, &K));
+  MB_REQUIRE(A->bytes == (size_t)(M * K * 4) && B->bytes == (size_t)(K * N * 4) &&
+                 Cb->bytes == (size_t)(M * N * 4),
+             "sqr_mm: buffer sizes do not match M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+             (long long)K);
+  const void *pa = A->dev, *pb = B->dev;
+  void* pc = Cb->dev;
+  st.threads_per_cta = 384;
+  st.smem_bytes = 197752;
+  st.launch = [=](cudaStream_t s) {
+    return mb_sqr_mm_f32((const float*)pa, (const float*)pb, (float*)pc, M, N, K, s);
+  };
+  return MB_OK;
+}
+
+// gemm_bf16: same bindings with bf16 buffers; config "b_layout" 0/1 (default 1).
+int prep_gemm_bf16(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *A, *B, *Cb;
+  int64_t M, N, K;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &A));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &B));
+  TRY(need_buf(a, 2, MB_ROLE_OUTPUT, &Cb));
+  TRY(need_scalar(a, 3, &M));
+  TRY(need_scalar(a, 4, &N));
+  TRY(need_scalar(a, 5, &K));
+  MB_REQUIRE(A->bytes == (size_t)(M * K * 2) && B->bytes == (size_t)(K * N * 2) &&
+                 Cb->bytes == (size_t)(M * N * 2),
+             "gemm_bf16: buffer sizes do not match");
+  const int lay = (int)a.config.num("b_layout", 1);
+  const void *pa = A->dev, *pb = B->dev;
+  void* pc = Cb->dev;
+  st.threads_per_cta = 256;
+  st.smem_bytes = 197752;
+  st.launch = [=](cudaStream_t s) {
+    return mb_gemm_bf16((const uint16_t*)pa, (const uint16_t*)pb, (uint16_t*)pc, M, N, K, lay, s);
+  };
+  return MB_OK;
+}
+
 }  // namespace
 
 void register_all_kernels() {
@@ -87,6 +136,8 @@ void register_all_kernels() {
   std::call_once(once, [] {
     register_kernel({"transpose_2d", prep_transpose_2d});
     register_kernel({"transpose_batched", prep_transpose_batched});
+    register_kernel({"sqr_mm", prep_sqr_mm});
+    register_kernel({"gemm_bf16", prep_gemm_bf16});
   });
 }
 

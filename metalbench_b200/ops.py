@@ -68,3 +68,44 @@ def transpose_batched(a: torch.Tensor, out: torch.Tensor | None = None) -> torch
     fn = "mb_transpose_batched_f32" if a.dtype == torch.float32 else "mb_transpose_batched_bf16"
     _lib.call(fn, a.data_ptr(), out.data_ptr(), Bn, R, Cc, _stream())
     return out
+
+
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+              b_layout: str = "kn") -> torch.Tensor:
+    """bf16 GEMM on the tcgen05 core. ``b_layout="kn"``: b is [K, N] (a @ b);
+    ``"nk"``: b is [N, K] (a @ b.T, the packed-weight layout)."""
+    _cuda(a, "gemm_bf16(a)", (torch.bfloat16,))
+    _cuda(b, "gemm_bf16(b)", (torch.bfloat16,))
+    init(a.device.index)
+    M, K = a.shape
+    if b_layout == "kn":
+        Kb, N = b.shape
+        lay = 1
+    elif b_layout == "nk":
+        N, Kb = b.shape
+        lay = 0
+    else:
+        raise ValueError("b_layout must be 'kn' or 'nk'")
+    if Kb != K:
+        raise ValueError(f"gemm_bf16: inner dimensions differ ({K} vs {Kb})")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    _cuda(out, "gemm_bf16(out)", (torch.bfloat16,))
+    _lib.call("mb_gemm_bf16", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, lay, _stream())
+    return out
+
+
+def sqr_mm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 C = A @ B (row-major), fp32-accurate 3xTF32 on the tensor cores."""
+    _cuda(a, "sqr_mm(a)", (torch.float32,))
+    _cuda(b, "sqr_mm(b)", (torch.float32,))
+    init(a.device.index)
+    M, K = a.shape
+    Kb, N = b.shape
+    if Kb != K:
+        raise ValueError(f"sqr_mm: inner dimensions differ ({K} vs {Kb})")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    _cuda(out, "sqr_mm(out)", (torch.float32,))
+    _lib.call("mb_sqr_mm_f32", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _stream())
+    return out
