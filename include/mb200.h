@@ -147,10 +147,13 @@ int mb_gemm_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, i
                  int64_t K, int b_layout, void* stream);
 
 /* C[M,N] (fp32) = A[M,K] @ B[K,N], all fp32 row-major, fp32-accurate via
- * 3xTF32 on the tensor cores (hi*hi + hi*lo + lo*hi, fp32 accumulate).
- * Needs K % 4 == 0, N % 4 == 0, 16-byte aligned pointers. */
+ * 3xTF32 on the tensor cores: a prepass writes tf32 hi/lo splits of A and of
+ * B^T into `workspace` (mb_sqr_mm_f32_workspace_bytes, 256-byte aligned, caller
+ * owned), then lo*hi + hi*lo + hi*hi accumulate in fp32 in TMEM.
+ * Needs K % 4 == 0 and a 16-byte aligned A. */
+size_t mb_sqr_mm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
-                  void* stream);
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

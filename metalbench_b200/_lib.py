@@ -65,7 +65,8 @@ SIGNATURES = {
     "mb_transpose_batched_bf16": (C.c_int, [_P, _P, _I64, _I64, _I64, _P]),
     "mb_transpose_batched_f32": (C.c_int, [_P, _P, _I64, _I64, _I64, _P]),
     "mb_gemm_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
-    "mb_sqr_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P]),
+    "mb_sqr_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64]),
+    "mb_sqr_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, C.c_size_t, _P]),
 }
 
 _lib = None

@@ -74,12 +74,92 @@ extern "C" int mb_gemm_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, i
   return launch_gemm<gemm::Mode::BF16, 256, 4, true>(A, B, e, M, N, K, 1, s);
 }
 
+namespace {
+
+// tf32 "hi" = the fp32 value with its low 13 mantissa bits cleared (exactly
+// representable in tf32, so the tensor core sees it unchanged); "lo" = the
+// exact fp32 remainder x - hi.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  lo = x - hi;
+}
+
+// A [M,K] -> A_hi, A_lo (same row-major layout), 16 bytes per thread step.
+__global__ void split_a_kernel(const float4* __restrict__ a, float4* __restrict__ hi,
+                               float4* __restrict__ lo, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 x = a[i];
+    float4 h, l;
+    split_tf32(x.x, h.x, l.x);
+    split_tf32(x.y, h.y, l.y);
+    split_tf32(x.z, h.z, l.z);
+    split_tf32(x.w, h.w, l.w);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// B [K,N] -> Bt_hi, Bt_lo [N,K] (transposed so both GEMM operands are K-major),
+// 32x32 tiles through a padded shared tile.
+__global__ void split_bt_kernel(const float* __restrict__ b, float* __restrict__ hi,
+                                float* __restrict__ lo, int64_t K, int64_t N) {
+  __shared__ float T[32][33];
+  const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int r = ty; r < 32; r += 8)
+    if (k0 + r < K && n0 + tx < N) T[r][tx] = b[(k0 + r) * N + n0 + tx];
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8)
+    if (n0 + r < N && k0 + tx < K) {
+      float h, l;
+      split_tf32(T[tx][r], h, l);
+      hi[(n0 + r) * K + k0 + tx] = h;
+      lo[(n0 + r) * K + k0 + tx] = l;
+    }
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" size_t mb_sqr_mm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return 2 * align256((size_t)M * K * 4) + 2 * align256((size_t)N * K * 4);
+}
+
 extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
-                             int64_t K, void* stream) {
+                             int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
   MB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "mb_sqr_mm_f32: negative dimension");
   if (M == 0 || N == 0) return MB_OK;
   MB_REQUIRE(K > 0, "mb_sqr_mm_f32: K must be positive");
-  MB_REQUIRE(N % 4 == 0 && K % 4 == 0, "mb_sqr_mm_f32: N and K must be multiples of 4");
+  MB_REQUIRE(K % 4 == 0, "mb_sqr_mm_f32: K must be a multiple of 4");
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0, "mb_sqr_mm_f32: A must be 16-byte aligned");
+  const size_t need = mb_sqr_mm_f32_workspace_bytes(M, N, K);
+  MB_REQUIRE(workspace != nullptr && workspace_bytes >= need &&
+                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "mb_sqr_mm_f32: workspace of %zu bytes (256-byte aligned) required, got %zu", need,
+             workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  float* a_hi = reinterpret_cast<float*>(w);
+  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)M * K * 4));
+  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4));
+  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4) +
+                                         align256((size_t)N * K * 4));
+  const int64_t n4 = M * K / 4;
+  const int sms = mb::num_sms();
+  split_a_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(A),
+                                          reinterpret_cast<float4*>(a_hi),
+                                          reinterpret_cast<float4*>(a_lo), n4);
+  MB_CUDA(cudaGetLastError());
+  dim3 g((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
+  MB_REQUIRE(g.y <= 65535, "mb_sqr_mm_f32: K too large");
+  split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
+  MB_CUDA(cudaGetLastError());
+
+  using P = GemmProducer<Mode::TF32X3, 128, false>;
+  using S = Smem<Mode::TF32X3, 128, 3>;
   gemm::Epi<128, gemm::EpiStore> e{};
   e.M = (int)M;
   e.N = (int)N;
@@ -87,6 +167,28 @@ extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M
   e.ldo = N;
   e.out_f32 = 1;
   e.alpha = 1.f;
-  return launch_gemm<gemm::Mode::TF32X3, 128, 3, true>(A, B, e, M, N, K, 1,
-                                                       static_cast<cudaStream_t>(stream));
+  P p;
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc = mb::make_tmap_2d(&p.a, a_hi, dt, 4, K, M, K * 4, P::KE, BM, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.alo, a_lo, dt, 4, K, M, K * 4, P::KE, BM, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.b, b_hi, dt, 4, K, N, K * 4, P::KE, 128, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.blo, b_lo, dt, 4, K, N, K * 4, P::KE, 128, sw);
+  if (rc) return rc;
+  Sched sc;
+  sc.tiles_m = (int)((M + BM - 1) / BM);
+  sc.tiles_n = (int)((N + 127) / 128);
+  sc.kblocks = (int)((K + P::KE - 1) / P::KE);
+  sc.ksplit = 1;
+  sc.kb_per_split = sc.kblocks;
+  auto kern = gemm_kernel<Mode::TF32X3, 128, 3, false, P, decltype(e)>;
+  static bool attr = false;
+  if (!attr) {
+    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr = true;
+  }
+  const int grid = sc.total() < sms ? sc.total() : sms;
+  kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, mb::device_status_ptr());
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
 }

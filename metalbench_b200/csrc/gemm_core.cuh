@@ -14,9 +14,9 @@
 //   warps 4-7   epilogue: tcgen05.ld the finished accumulator (warp w owns
 //               TMEM lanes 32*(w%4)..+31 = tile rows), apply the fused
 //               epilogue functor, store; then hand the accumulator back.
-//   warps 8-11  (TF32x3 mode only) split every fp32 tile in shared memory into
-//               a tf32 "hi" part (low 13 mantissa bits cleared) and the exact
-//               remainder "lo", so the MMA warp can issue hi*hi + hi*lo + lo*hi.
+// TF32x3 mode streams four K-major fp32 operands per stage (A_hi, B_hi, A_lo,
+// B_lo, produced by a split prepass: hi = low 13 mantissa bits cleared, lo =
+// the exact remainder) and issues lo*hi + hi*lo + hi*hi per k-step.
 // With two accumulators the epilogue of tile i overlaps the main loop of
 // tile i+1. Every mbarrier wait is bounded (common.cuh) and reports through
 // the device status word instead of hanging.
@@ -31,17 +31,17 @@ constexpr int KBYTES = 128;  // K extent of one stage in bytes (one swizzle row)
 enum class Mode { BF16 = 0, TF32X3 = 1 };
 
 __host__ __device__ constexpr int elem_bytes(Mode m) { return m == Mode::BF16 ? 2 : 4; }
-__host__ __device__ constexpr int num_warps(Mode m) { return m == Mode::TF32X3 ? 12 : 8; }
+__host__ __device__ constexpr int num_warps(Mode) { return 8; }
 
 template <Mode MODE, int BN, int STAGES>
 struct Smem {
   static constexpr int A_BYTES = BM * KBYTES;
   static constexpr int B_BYTES = BN * KBYTES;
-  static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;  // raw/hi (+ lo)
+  static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;  // hi (+ lo)
   static constexpr int STAGE_BYTES = PARTS * (A_BYTES + B_BYTES);
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  // barriers: full, ready (after split), empty per stage; tfull, tempty x2
-  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
+  // barriers: full, empty per stage; tfull, tempty x2; tmem slot, abort, drain
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
   static constexpr int TOTAL = 1024 /*alignment slack*/ + RING_BYTES + BAR_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
 };
@@ -90,15 +90,24 @@ struct EpiCtx {
 // ---------------------------------------------------------------------------
 template <Mode MODE, int BN, bool B_MN>
 struct GemmProducer {
-  CUtensorMap a, b;
+  CUtensorMap a, b, alo, blo;  // alo / blo: TF32x3 remainders (K-major)
   static constexpr int KE = KBYTES / elem_bytes(MODE);  // K elements per stage
-  static constexpr uint32_t BYTES = (BM + BN) * KBYTES;
+  static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;
+  static constexpr uint32_t BYTES = PARTS * (BM + BN) * KBYTES;
   static constexpr int B_BOX_BYTES = KE * KBYTES;       // one MN-major box
+  static_assert(MODE == Mode::BF16 || !B_MN, "TF32x3 operands are K-major");
   __device__ void prefetch() const {
     mbd::prefetch_tmap(&a);
     mbd::prefetch_tmap(&b);
+    if constexpr (MODE == Mode::TF32X3) {
+      mbd::prefetch_tmap(&alo);
+      mbd::prefetch_tmap(&blo);
+    }
   }
-  __device__ void load(uint8_t* sA, uint8_t* sB, uint64_t* bar, int tm, int tn, int kb) const {
+  // Stage layout: [A hi][B hi]([A lo][B lo]).
+  __device__ void load(uint8_t* st, uint64_t* bar, int tm, int tn, int kb) const {
+    uint8_t* sA = st;
+    uint8_t* sB = st + BM * KBYTES;
     mbd::tma_load_2d(sA, &a, bar, kb * KE, tm * BM);
     if constexpr (!B_MN) {
       mbd::tma_load_2d(sB, &b, bar, kb * KE, tn * BN);
@@ -106,6 +115,10 @@ struct GemmProducer {
 #pragma unroll
       for (int j = 0; j < BN / KE; ++j)
         mbd::tma_load_2d(sB + j * B_BOX_BYTES, &b, bar, tn * BN + j * KE, kb * KE);
+    }
+    if constexpr (MODE == Mode::TF32X3) {
+      mbd::tma_load_2d(sB + BN * KBYTES, &alo, bar, kb * KE, tm * BM);
+      mbd::tma_load_2d(sB + BN * KBYTES + BM * KBYTES, &blo, bar, kb * KE, tn * BN);
     }
   }
   // Shared-memory descriptors for MMA k-step kk of a stage.
@@ -130,8 +143,7 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(base + S::RING_BYTES);
-  uint64_t* ready = full + STAGES;
-  uint64_t* empty = ready + STAGES;
+  uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
@@ -141,14 +153,13 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto sA = [&](int s) { return base + s * S::STAGE_BYTES; };
   auto sB = [&](int s) { return base + s * S::STAGE_BYTES + S::A_BYTES; };
-  // TF32x3: the "lo" halves follow the raw/hi halves of the stage.
+  // TF32x3: the "lo" halves follow the hi halves of the stage.
   auto sAlo = [&](int s) { return base + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
   auto sBlo = [&](int s) { return base + s * S::STAGE_BYTES + 2 * S::A_BYTES + S::B_BYTES; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbd::mbar_init(&full[s], 1);
-      mbd::mbar_init(&ready[s], 128);
       mbd::mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -184,7 +195,7 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
             break;
           }
           mbd::mbar_expect_tx(&full[stage], Producer::BYTES);
-          prod.load(sA(stage), sB(stage), &full[stage], tm, tn, kb);
+          prod.load(sA(stage), &full[stage], tm, tn, kb);
           issued = (issued & ~(1u << stage)) | (phase << stage);
           used |= 1u << stage;
           if (++stage == STAGES) {
@@ -217,8 +228,7 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
         mbd::tc_fence_after();
         const uint32_t d = tmem + buf * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          uint64_t* gate = MODE == Mode::TF32X3 ? &ready[stage] : &full[stage];
-          if (!mbd::mbar_wait(gate, phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
+          if (!mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
             ok = false;
             break;
           }
@@ -270,49 +280,6 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
       epi(c);
       mbd::tc_fence_before();
       mbd::mbar_arrive(&tempty[buf]);
-    }
-  } else if (MODE == Mode::TF32X3 && warp >= 8) {
-    // ---------------- fp32 -> tf32 hi + lo splitter ----------------
-    const int ct = threadIdx.x - 256;  // 0..127
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-      int tm, tn, ks, kb0, kb1;
-      sched.get(t, tm, tn, ks);
-      sched.krange(ks, kb0, kb1);
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
-          ok = false;
-          break;
-        }
-        // A (hi in place, lo behind B) then B: position-preserving, so the
-        // swizzle of the tile does not matter.
-        uint4* ra = reinterpret_cast<uint4*>(sA(stage));
-        uint4* la = reinterpret_cast<uint4*>(sAlo(stage));
-        constexpr int NA = S::A_BYTES / 16, NB = S::B_BYTES / 16;
-        for (int v = ct; v < NA + NB; v += 128) {
-          uint4* r = v < NA ? ra + v : reinterpret_cast<uint4*>(sB(stage)) + (v - NA);
-          uint4* l = v < NA ? la + v : reinterpret_cast<uint4*>(sBlo(stage)) + (v - NA);
-          uint4 x = *r, hi, lo;
-          hi.x = x.x & 0xFFFFE000u;
-          hi.y = x.y & 0xFFFFE000u;
-          hi.z = x.z & 0xFFFFE000u;
-          hi.w = x.w & 0xFFFFE000u;
-          lo.x = __float_as_uint(__uint_as_float(x.x) - __uint_as_float(hi.x));
-          lo.y = __float_as_uint(__uint_as_float(x.y) - __uint_as_float(hi.y));
-          lo.z = __float_as_uint(__uint_as_float(x.z) - __uint_as_float(hi.z));
-          lo.w = __float_as_uint(__uint_as_float(x.w) - __uint_as_float(hi.w));
-          *r = hi;
-          *l = lo;
-        }
-        mbd::fence_proxy_async();  // generic-proxy writes -> visible to tcgen05
-        mbd::mbar_arrive(&ready[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
     }
   }
   __syncthreads();

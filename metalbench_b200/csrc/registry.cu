@@ -97,10 +97,17 @@ int prep_sqr_mm(const RunArgs& a, KernelState& st, cudaStream_t) {
              (long long)K);
   const void *pa = A->dev, *pb = B->dev;
   void* pc = Cb->dev;
-  st.threads_per_cta = 384;
+  const size_t wsb = mb_sqr_mm_f32_workspace_bytes(M, N, K);
+  void* ws = nullptr;
+  if (wsb) {
+    MB_CUDA(cudaMalloc(&ws, wsb));
+    st.scratch.push_back(ws);
+  }
+  st.threads_per_cta = 256;
   st.smem_bytes = 197752;
+  st.launches_per_iter = 3;
   st.launch = [=](cudaStream_t s) {
-    return mb_sqr_mm_f32((const float*)pa, (const float*)pb, (float*)pc, M, N, K, s);
+    return mb_sqr_mm_f32((const float*)pa, (const float*)pb, (float*)pc, M, N, K, ws, wsb, s);
   };
   return MB_OK;
 }

@@ -107,5 +107,21 @@ def sqr_mm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) ->
     if out is None:
         out = torch.empty((M, N), dtype=torch.float32, device=a.device)
     _cuda(out, "sqr_mm(out)", (torch.float32,))
-    _lib.call("mb_sqr_mm_f32", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _stream())
+    ws_bytes = _lib.lib().mb_sqr_mm_f32_workspace_bytes(M, N, K)
+    ws = _workspace(ws_bytes, a.device)
+    _lib.call("mb_sqr_mm_f32", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
+              ws.data_ptr() if ws_bytes else None, ws_bytes, _stream())
     return out
+
+
+_ws: dict = {}
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    """Per-device scratch tensor, grown on demand (256-byte aligned by torch)."""
+    key = device.index
+    t = _ws.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _ws[key] = t
+    return t
