@@ -155,6 +155,23 @@ size_t mb_sqr_mm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* sqr_mm for callers that cannot allocate device memory. This entry point
+ * has no counterpart in the reference. It computes exactly what
+ * mb_sqr_mm_f32 computes, but takes its scratch from a 64 MiB array compiled
+ * into the library (held on every GPU that loads it, until exit) instead of a
+ * caller workspace, and calls no allocator (no cudaMalloc, no torch).
+ *  - Shapes whose scratch (mb_sqr_mm_f32_workspace_bytes) exceeds
+ *    mb_sqr_mm_f32_noalloc_max_workspace_bytes() are rejected with
+ *    MB_ERR_BAD_ARG; 2048^3 fits.
+ *  - The first call on a device looks up the array's device address with
+ *    cudaGetSymbolAddress, so make it before any stream capture.
+ *  - All calls share the one array: calls that overlap on the GPU (different
+ *    streams, or other processes' threads on the same context) race and give
+ *    wrong results. Serialise them, e.g. on one stream. */
+size_t mb_sqr_mm_f32_noalloc_max_workspace_bytes(void);
+int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                          int64_t K, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

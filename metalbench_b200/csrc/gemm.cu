@@ -192,3 +192,117 @@ extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
+
+// ---------------------------------------------------------------------------
+// sqr_mm without any allocation.
+//
+// Some callers cannot allocate device memory at all: a plugin that runs
+// inside a host process which owns every allocation (a custom allocator or
+// a memory pool it must not bypass), or code that must not call cudaMalloc
+// because an allocation would synchronise the device or fail under a memory
+// cap. They still need the scratch that mb_sqr_mm_f32 takes as `workspace`.
+// This entry point takes it from a fixed array compiled into the library
+// instead: every GPU that loads libmb200.so holds these 64 MiB until the
+// process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB: enough for 2048^3
+static __device__ __align__(256) uint8_t g_sqr_mm_scratch[kNoAllocScratchBytes];
+static __device__ uint32_t g_sqr_mm_scratch_status;
+
+// Device addresses of the two arrays, looked up once per device (the names
+// are host-side stand-ins, never device addresses).
+struct NoAllocSlot {
+  void* scratch = nullptr;
+  uint32_t* status = nullptr;
+};
+constexpr int kMaxDevices = 64;
+NoAllocSlot g_noalloc[kMaxDevices];
+
+int noalloc_setup(int dev, NoAllocSlot** out) {
+  MB_REQUIRE(dev >= 0 && dev < kMaxDevices, "mb_sqr_mm_f32_noalloc: device %d out of range", dev);
+  NoAllocSlot& s = g_noalloc[dev];
+  if (!s.scratch) {
+    void* p = nullptr;
+    void* q = nullptr;
+    MB_CUDA(cudaGetSymbolAddress(&p, g_sqr_mm_scratch));
+    MB_CUDA(cudaGetSymbolAddress(&q, g_sqr_mm_scratch_status));
+    s.status = static_cast<uint32_t*>(q);
+    s.scratch = p;
+  }
+  *out = &s;
+  return MB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t mb_sqr_mm_f32_noalloc_max_workspace_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, int64_t M,
+                                     int64_t N, int64_t K, void* stream) {
+  MB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "mb_sqr_mm_f32_noalloc: negative dimension");
+  if (M == 0 || N == 0) return MB_OK;
+  MB_REQUIRE(K > 0 && K % 4 == 0, "mb_sqr_mm_f32_noalloc: K must be a positive multiple of 4");
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0,
+             "mb_sqr_mm_f32_noalloc: A must be 16-byte aligned");
+  const size_t need = mb_sqr_mm_f32_workspace_bytes(M, N, K);
+  MB_REQUIRE(need <= kNoAllocScratchBytes,
+             "mb_sqr_mm_f32_noalloc: M=%lld N=%lld K=%lld needs %zu bytes of scratch, more than "
+             "the fixed %zu-byte array; use mb_sqr_mm_f32 with a caller workspace",
+             (long long)M, (long long)N, (long long)K, need, kNoAllocScratchBytes);
+  int dev = 0;
+  MB_CUDA(cudaGetDevice(&dev));
+  NoAllocSlot* slot = nullptr;
+  int rc = noalloc_setup(dev, &slot);
+  if (rc) return rc;
+
+  // The split prepass overwrites every scratch byte the GEMM reads, so nothing
+  // has to be cleared first.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(slot->scratch);
+  float* a_hi = reinterpret_cast<float*>(w);
+  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)M * K * 4));
+  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4));
+  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4) +
+                                         align256((size_t)N * K * 4));
+  const int sms = mb::num_sms();
+  split_a_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(A),
+                                          reinterpret_cast<float4*>(a_hi),
+                                          reinterpret_cast<float4*>(a_lo), M * K / 4);
+  MB_CUDA(cudaGetLastError());
+  dim3 g((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
+  MB_REQUIRE(g.y <= 65535, "mb_sqr_mm_f32_noalloc: K too large");
+  split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
+  MB_CUDA(cudaGetLastError());
+
+  using P = GemmProducer<Mode::TF32X3, 128, false>;
+  using S = Smem<Mode::TF32X3, 128, 3>;
+  gemm::Epi<128, gemm::EpiStore> e{};
+  e.M = (int)M;
+  e.N = (int)N;
+  e.out = C;
+  e.ldo = N;
+  e.out_f32 = 1;
+  e.alpha = 1.f;
+  P p;
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  rc = mb::make_tmap_2d(&p.a, a_hi, dt, 4, K, M, K * 4, P::KE, BM, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.alo, a_lo, dt, 4, K, M, K * 4, P::KE, BM, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.b, b_hi, dt, 4, K, N, K * 4, P::KE, 128, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.blo, b_lo, dt, 4, K, N, K * 4, P::KE, 128, sw);
+  if (rc) return rc;
+  Sched sc;
+  sc.tiles_m = (int)((M + BM - 1) / BM);
+  sc.tiles_n = (int)((N + 127) / 128);
+  sc.kblocks = (int)((K + P::KE - 1) / P::KE);
+  sc.ksplit = 1;
+  sc.kb_per_split = sc.kblocks;
+  auto kern = gemm_kernel<Mode::TF32X3, 128, 3, false, P, decltype(e)>;
+  MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+  const int grid = sc.total() < sms ? sc.total() : sms;
+  kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, slot->status);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
