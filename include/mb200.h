@@ -155,6 +155,17 @@ size_t mb_sqr_mm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- conv2d (hook mlx/kernels/common/conv2d.py:7-12; registry
+ *      mlx/kernels/common/registry.py:469-477; Metal kernel
+ *      metal/kernels/common/conv2d/default.metal:31-217) ------------------ */
+
+/* y = conv2d(x, w): x NHWC [N,H,W,Cin] bf16, w OHWI [Cout,KH,KW,Cin] bf16,
+ * cross-correlation, symmetric zero padding `pad`, y NHWC [N,H2,W2,Cout] bf16
+ * with fp32 accumulation. Needs stride 1, Cin % 64 == 0, Cout % 16 == 0,
+ * Cout <= 256, pad < KH and pad < KW, 16-byte aligned pointers. */
+int mb_conv2d_nhwc_bf16(const uint16_t* x, const uint16_t* w, uint16_t* y, int N, int H, int W,
+                        int Cin, int Cout, int KH, int KW, int stride, int pad, void* stream);
+
 /* sqr_mm for callers that cannot allocate device memory. This entry point
  * has no counterpart in the reference. It computes exactly what
  * mb_sqr_mm_f32 computes, but takes its scratch from a 64 MiB array compiled

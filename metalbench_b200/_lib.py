@@ -67,6 +67,7 @@ SIGNATURES = {
     "mb_gemm_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "mb_sqr_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64]),
     "mb_sqr_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, C.c_size_t, _P]),
+    "mb_conv2d_nhwc_bf16": (C.c_int, [_P, _P, _P] + [_I] * 9 + [_P]),
     "mb_sqr_mm_f32_noalloc_max_workspace_bytes": (C.c_size_t, []),
     "mb_sqr_mm_f32_noalloc": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P]),
 }

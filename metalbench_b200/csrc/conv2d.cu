@@ -1,0 +1,152 @@
+// NHWC conv2d (cross-correlation, OHWI weights) as an implicit GEMM on the
+// tcgen05 core.
+//
+// Reference: hook mlx/kernels/common/conv2d.py:7-12 (mx.conv2d, NHWC x OHWI,
+// stride, padding 0 in the hook; the north-star config uses padding 1), the
+// registry entry mlx/kernels/common/registry.py:469-477 and the Metal kernel
+// metal/kernels/common/conv2d/default.metal:31-217 (implicit im2col GEMM with
+// M = N*H2*W2, K = KH*KW*Cin, simdgroup MMA).
+//
+//   GEMM M  = output pixels, tiled as TH output rows x TW output columns of one
+//            image (TH*TW = 128; TW = 64 when W2 <= 64, else 128);
+//   GEMM N  = Cout (one N tile of up to 256);
+//   GEMM K  = (r, s, c): one k-block is one filter tap (r, s) x 64 channels.
+// The A tile of a k-block is ONE 4-D TMA box {64 ch, TW, TH, 1} of x taken at
+// (c0, w0 + s - pad, h0 + r - pad, n): TMA zero-fills coordinates outside the
+// image, which is exactly the zero padding, and lands the box as 128 rows of
+// 128 bytes in the same 128-byte swizzle as a K-major GEMM operand. The weight
+// tensor [Cout, KH*KW*Cin] is the K-major B operand as stored (OHWI).
+#include "gemm_core.cuh"
+#include "gemm_epi.cuh"
+
+namespace {
+
+using namespace gemm;
+
+struct ConvGeom {
+  int N, H, W, C, Co, KH, KW, pad, H2, W2, TH, TW, tiles_h, tiles_w, cchunks;
+};
+
+template <int BN>
+struct ConvProducer {
+  CUtensorMap x, w;
+  ConvGeom g;
+  static constexpr int KE = 64;
+  static constexpr uint32_t BYTES = (BM + BN) * KBYTES;
+  static constexpr int KSTEPS = 4;
+  __device__ void prefetch() const {
+    mbd::prefetch_tmap(&x);
+    mbd::prefetch_tmap(&w);
+  }
+  __device__ void load(uint8_t* st, uint64_t* bar, int tm, int tn, int kb) const {
+    const int tw = tm % g.tiles_w;
+    const int th = (tm / g.tiles_w) % g.tiles_h;
+    const int n = tm / (g.tiles_w * g.tiles_h);
+    const int tap = kb / g.cchunks, c0 = (kb % g.cchunks) * 64;
+    const int r = tap / g.KW, s = tap % g.KW;
+    mbd::tma_load_4d(st, &x, bar, c0, tw * g.TW + s - g.pad, th * g.TH + r - g.pad, n);
+    mbd::tma_load_2d(st + BM * KBYTES, &w, bar, kb * 64, tn * BN);
+  }
+  __device__ static uint64_t a_desc(uint32_t sA, int kk) {
+    return mbd::sw128_desc(sA + kk * 32, 16, 1024);
+  }
+  __device__ static uint64_t b_desc(uint32_t sB, int kk) {
+    return mbd::sw128_desc(sB + kk * 32, 16, 1024);
+  }
+};
+
+// Accumulator row (hh * TW + ww) of tile tm is output pixel
+// (n, th*TH + hh, tw*TW + ww); rows past the image edge are dropped.
+template <int BN>
+struct EpiConv {
+  int M;  // tiles_m * 128: every accumulator row is "in range" for the core
+  ConvGeom g;
+  uint16_t* y;
+  __device__ void operator()(const EpiCtx& c) const {
+    const int tm = c.row / BM, local = c.row % BM;
+    const int tw = tm % g.tiles_w;
+    const int th = (tm / g.tiles_w) % g.tiles_h;
+    const int n = tm / (g.tiles_w * g.tiles_h);
+    const int h = th * g.TH + local / g.TW, wo = tw * g.TW + local % g.TW;
+    const bool ok = h < g.H2 && wo < g.W2;
+    const int64_t pix = ((int64_t)n * g.H2 + h) * g.W2 + wo;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld32(c.taddr + c0, v);
+      const int nn = c.n0 + c0;
+      if (!ok || nn >= g.Co) continue;
+      store_row32(y, g.Co, 0, (int)pix, nn, g.Co, v);
+    }
+  }
+};
+
+template <int BN, int STAGES>
+int launch_conv(const uint16_t* x, const uint16_t* w, uint16_t* y, const ConvGeom& g,
+                cudaStream_t stream) {
+  using S = Smem<Mode::BF16, BN, STAGES>;
+  using P = ConvProducer<BN>;
+  using E = EpiConv<BN>;
+  P p;
+  p.g = g;
+  const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+  const uint64_t strides[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2,
+                               (uint64_t)g.H * g.W * g.C * 2};
+  const uint32_t box[4] = {64, (uint32_t)g.TW, (uint32_t)g.TH, 1};
+  int rc = mb::make_tmap_nd(&p.x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const int64_t Kt = (int64_t)g.KH * g.KW * g.C;
+  rc = mb::make_tmap_2d(&p.w, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Kt, g.Co, Kt * 2, 64, BN,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  Sched sc;
+  sc.tiles_m = g.N * g.tiles_h * g.tiles_w;
+  sc.tiles_n = (g.Co + BN - 1) / BN;
+  sc.kblocks = g.KH * g.KW * g.cchunks;
+  sc.ksplit = 1;
+  sc.kb_per_split = sc.kblocks;
+  E e;
+  e.M = sc.tiles_m * BM;
+  e.g = g;
+  e.y = y;
+  auto kern = gemm_kernel<Mode::BF16, BN, STAGES, false, P, E>;
+  static bool attr = false;
+  if (!attr) {
+    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr = true;
+  }
+  const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
+  kern<<<grid, 256, S::TOTAL, stream>>>(p, e, sc, mb::device_status_ptr());
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+}  // namespace
+
+extern "C" int mb_conv2d_nhwc_bf16(const uint16_t* x, const uint16_t* w, uint16_t* y, int N, int H,
+                                   int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
+                                   void* stream) {
+  MB_REQUIRE(N >= 0 && H > 0 && W > 0 && KH > 0 && KW > 0 && pad >= 0,
+             "mb_conv2d_nhwc_bf16: bad geometry");
+  MB_REQUIRE(stride == 1, "mb_conv2d_nhwc_bf16: only stride 1 is implemented (got %d)", stride);
+  MB_REQUIRE(Cin > 0 && Cin % 64 == 0, "mb_conv2d_nhwc_bf16: Cin must be a multiple of 64");
+  MB_REQUIRE(Cout > 0 && Cout % 16 == 0 && Cout <= 256,
+             "mb_conv2d_nhwc_bf16: Cout must be a multiple of 16 and at most 256");
+  MB_REQUIRE(pad < KH && pad < KW, "mb_conv2d_nhwc_bf16: padding must be smaller than the kernel");
+  ConvGeom g;
+  g.N = N; g.H = H; g.W = W; g.C = Cin; g.Co = Cout; g.KH = KH; g.KW = KW; g.pad = pad;
+  g.H2 = H + 2 * pad - KH + 1;
+  g.W2 = W + 2 * pad - KW + 1;
+  MB_REQUIRE(g.H2 > 0 && g.W2 > 0, "mb_conv2d_nhwc_bf16: empty output");
+  if (N == 0) return MB_OK;
+  g.TW = g.W2 <= 64 ? 64 : 128;
+  g.TH = BM / g.TW;
+  g.tiles_w = (g.W2 + g.TW - 1) / g.TW;
+  g.tiles_h = (g.H2 + g.TH - 1) / g.TH;
+  g.cchunks = Cin / 64;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (Cout <= 64) return launch_conv<64, 8>(x, w, y, g, s);
+  if (Cout <= 128) return launch_conv<128, 6>(x, w, y, g, s);
+  return launch_conv<256, 4>(x, w, y, g, s);
+}

@@ -136,6 +136,43 @@ int prep_gemm_bf16(const RunArgs& a, KernelState& st, cudaStream_t) {
   return MB_OK;
 }
 
+// conv2d: registry common/registry.py:469-477 — x@0, w@1, y@2, N@3, H@4, W@5,
+// Cin@6, Cout@7, KH@8, KW@9, stride@10; padding from scalar 11 or config
+// "padding" (the reference hook hard-codes 0).
+int prep_conv2d(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *w, *y;
+  int64_t N, H, W, Ci, Co, KH, KW, stride;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &w));
+  TRY(need_buf(a, 2, MB_ROLE_OUTPUT, &y));
+  TRY(need_scalar(a, 3, &N));
+  TRY(need_scalar(a, 4, &H));
+  TRY(need_scalar(a, 5, &W));
+  TRY(need_scalar(a, 6, &Ci));
+  TRY(need_scalar(a, 7, &Co));
+  TRY(need_scalar(a, 8, &KH));
+  TRY(need_scalar(a, 9, &KW));
+  TRY(need_scalar(a, 10, &stride));
+  double padv = a.config.num("padding", 0);
+  a.scalar(11, &padv);
+  const int64_t pad = (int64_t)padv;
+  MB_REQUIRE(x->dtype == MB_BF16 && w->dtype == MB_BF16 && y->dtype == MB_BF16,
+             "conv2d: buffers must be bf16");
+  const int64_t H2 = H + 2 * pad - KH + 1, W2 = W + 2 * pad - KW + 1;
+  MB_REQUIRE(x->bytes == (size_t)(N * H * W * Ci * 2) && w->bytes == (size_t)(Co * KH * KW * Ci * 2) &&
+                 y->bytes == (size_t)(N * H2 * W2 * Co * 2),
+             "conv2d: buffer sizes do not match the geometry");
+  const void *px = x->dev, *pw = w->dev;
+  void* py = y->dev;
+  st.threads_per_cta = 256;
+  st.launch = [=](cudaStream_t s) {
+    return mb_conv2d_nhwc_bf16((const uint16_t*)px, (const uint16_t*)pw, (uint16_t*)py, (int)N,
+                               (int)H, (int)W, (int)Ci, (int)Co, (int)KH, (int)KW, (int)stride,
+                               (int)pad, s);
+  };
+  return MB_OK;
+}
+
 }  // namespace
 
 void register_all_kernels() {
@@ -145,6 +182,7 @@ void register_all_kernels() {
     register_kernel({"transpose_batched", prep_transpose_batched});
     register_kernel({"sqr_mm", prep_sqr_mm});
     register_kernel({"gemm_bf16", prep_gemm_bf16});
+    register_kernel({"conv2d", prep_conv2d});
   });
 }
 

@@ -125,3 +125,23 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
         t = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
         _ws[key] = t
     return t
+
+
+def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, stride: int = 1, padding: int = 0,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 NHWC x OHWI conv2d (cross-correlation) as a tcgen05 implicit GEMM."""
+    _cuda(x, "conv2d(x)", (torch.bfloat16,))
+    _cuda(w, "conv2d(w)", (torch.bfloat16,))
+    init(x.device.index)
+    N, H, W, C = x.shape
+    Co, KH, KW, Ci = w.shape
+    if Ci != C:
+        raise ValueError(f"conv2d: channel mismatch ({C} vs {Ci})")
+    H2 = (H + 2 * padding - KH) // stride + 1
+    W2 = (W + 2 * padding - KW) // stride + 1
+    if out is None:
+        out = torch.empty((N, H2, W2, Co), dtype=torch.bfloat16, device=x.device)
+    _cuda(out, "conv2d(out)", (torch.bfloat16,))
+    _lib.call("mb_conv2d_nhwc_bf16", x.data_ptr(), w.data_ptr(), out.data_ptr(), N, H, W, C, Co,
+              KH, KW, stride, padding, _stream())
+    return out
