@@ -166,6 +166,66 @@ int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N
 int mb_conv2d_nhwc_bf16(const uint16_t* x, const uint16_t* w, uint16_t* y, int N, int H, int W,
                         int Cin, int Cout, int KH, int KW, int stride, int pad, void* stream);
 
+/* ---- GQA attention over a paged KV cache (hook
+ *      mlx/kernels/full/llama_decoder_layer.py:30-37) ----------------------
+ * Cache: k_cache, v_cache = [num_pages][Hkv][64][Dh] bf16; token p of
+ * sequence b is in page block_table[b*max_pages + p/64], slot p%64. Query
+ * head h reads kv head h / (Hq/Hkv). Dh must be 128. */
+
+/* Decode: one query row per sequence (q [B, ldq]), keys 0..kv_len[b]-1.
+ * Split-KV; needs mb_attention_decode_workspace_bytes of caller scratch. */
+size_t mb_attention_decode_workspace_bytes(int B, int Hq, int Hkv, int max_kv_len);
+int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16_t* k_cache,
+                             const uint16_t* v_cache, const int* block_table, int max_pages,
+                             const int* kv_len, int max_kv_len, int B, int Hq, int Hkv, int Dh,
+                             uint16_t* out, int ldo, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* Prefill: S query rows per sequence (row b*S+s at position start_pos[b]+s),
+ * keys 0..kv_len[b]-1, optional causal mask (key position <= query position). */
+int mb_attention_prefill_bf16(const uint16_t* q, int ldq, const uint16_t* k_cache,
+                              const uint16_t* v_cache, const int* block_table, int max_pages,
+                              const int* start_pos, const int* kv_len, int B, int S, int Hq,
+                              int Hkv, int Dh, int causal, uint16_t* out, int ldo, void* stream);
+
+/* ---- LLaMA decoder layer (hook mlx/kernels/full/llama_decoder_layer.py:17-64;
+ *      registry mlx/kernels/full/registry.py:87-104; Metal kernel
+ *      metal/kernels/full/llama_decoder_layer/default.metal:16-206) ------- */
+typedef struct mb_decoder_config {
+  int d_model;
+  int n_heads;
+  int n_kv_heads;
+  int head_dim; /* must be 128 */
+  int ffn;
+  float rope_base;
+  float eps;
+} mb_decoder_config;
+
+/* Pack the reference-layout weights (device pointers, bf16, (in, out)
+ * row-major: W_qkv [D, D+2*Hkv*Dh], W_o [D, D], W_gu [D, 2*ffn] (gate | up),
+ * W_down [ffn, D]) into this rank's tensor-parallel shard (tp_world = 1 for one
+ * GPU). The layer owns its packed copies; the inputs may be freed after. */
+int mb_decoder_layer_create(const mb_decoder_config* cfg, const uint16_t* W_qkv,
+                            const uint16_t* W_o, const uint16_t* W_gu, const uint16_t* W_down,
+                            int tp_rank, int tp_world, void** layer);
+void mb_decoder_layer_destroy(void* layer);
+size_t mb_decoder_layer_workspace_bytes(const void* layer, int B, int S, int max_kv_len);
+
+/* y = layer(x) for B sequences of S new tokens (x, y [B*S, D] bf16, row b*S+s
+ * at position start_pos[b]+s). The new tokens' rotated K and V are written into
+ * the cache first; attention then reads keys 0..kv_len[b]-1 (= start_pos[b]+S),
+ * causal or not (the reference hook is non-causal with start_pos 0). S == 1
+ * uses the split-KV decode kernel. With tp_world > 1 (after mb_init with the
+ * same world) the o-proj and down-proj outputs are summed with NCCL. */
+int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, int B, int S,
+                             const int* start_pos, const int* kv_len, int max_kv_len,
+                             uint16_t* k_cache, uint16_t* v_cache, const int* block_table,
+                             int max_pages, int causal, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* In-place bf16 sum all-reduce over the tensor-parallel communicator. */
+int mb_tp_allreduce_bf16(uint16_t* buf, size_t count, void* stream);
+
 /* sqr_mm for callers that cannot allocate device memory. This entry point
  * has no counterpart in the reference. It computes exactly what
  * mb_sqr_mm_f32 computes, but takes its scratch from a 64 MiB array compiled

@@ -43,6 +43,12 @@ class MbDevice(C.Structure):
                 ("l2_bytes", C.c_int), ("smem_per_block_optin", C.c_int)]
 
 
+class MbDecoderConfig(C.Structure):
+    _fields_ = [("d_model", C.c_int), ("n_heads", C.c_int), ("n_kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("rope_base", C.c_float),
+                ("eps", C.c_float)]
+
+
 class MbError(RuntimeError):
     def __init__(self, fn: str, rc: int, msg: str):
         super().__init__(f"{fn} failed: MB_ERR_{MB_ERR.get(rc, rc)}: {msg}")
@@ -68,6 +74,18 @@ SIGNATURES = {
     "mb_sqr_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64]),
     "mb_sqr_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, C.c_size_t, _P]),
     "mb_conv2d_nhwc_bf16": (C.c_int, [_P, _P, _P] + [_I] * 9 + [_P]),
+    "mb_attention_decode_workspace_bytes": (C.c_size_t, [_I, _I, _I, _I]),
+    "mb_attention_decode_bf16": (C.c_int, [_P, _I, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _I,
+                                           _P, C.c_size_t, _P]),
+    "mb_attention_prefill_bf16": (C.c_int, [_P, _I, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I,
+                                            _P, _I, _P]),
+    "mb_decoder_layer_create": (C.c_int, [C.POINTER(MbDecoderConfig), _P, _P, _P, _P, _I, _I,
+                                          C.POINTER(C.c_void_p)]),
+    "mb_decoder_layer_destroy": (None, [_P]),
+    "mb_decoder_layer_workspace_bytes": (C.c_size_t, [_P, _I, _I, _I]),
+    "mb_decoder_layer_forward": (C.c_int, [_P, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _I, _I, _P,
+                                           C.c_size_t, _P]),
+    "mb_tp_allreduce_bf16": (C.c_int, [_P, C.c_size_t, _P]),
     "mb_sqr_mm_f32_noalloc_max_workspace_bytes": (C.c_size_t, []),
     "mb_sqr_mm_f32_noalloc": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P]),
 }

@@ -1,0 +1,443 @@
+// LLaMA decoder layer on B200: packed weights, fused tcgen05 GEMM epilogues,
+// paged-KV attention, optional tensor parallelism over NCCL.
+//
+// Reference: mlx/kernels/full/llama_decoder_layer.py:24-64 (hook) and
+// metal/kernels/full/llama_decoder_layer/default.metal:16-206 (one
+// threadgroup computing the whole layer). Here one layer forward is:
+//
+//   rstd1   = rownorm(x)                      (1 small kernel)
+//   q, K, V = RoPE((x @ Wqkv) * rstd1)         (GEMM + QKV epilogue: q -> [T, Dq],
+//                                               k, v scattered into the paged cache)
+//   a       = attention(q, cache)              (prefill: flash tiles; decode: split-KV)
+//   x1      = x + a @ Wo                       (GEMM + residual epilogue; TP: all-reduce)
+//   rstd2   = rownorm(x1)
+//   act     = silu(g) * u, [g|u] = (x1 @ Wgu) * rstd2   (GEMM + SwiGLU epilogue)
+//   y       = x1 + act @ Wdown                 (GEMM + residual epilogue; TP: all-reduce)
+//
+// The RMSNorm has no gain vector in the reference, so h @ W = rstd * (x @ W)
+// and the normalised activations never touch HBM. Weights are packed once, at
+// layer creation, into K-major [out, in] bf16 (both tcgen05 operands K-major);
+// the gate/up weight is interleaved in blocks of 128 gate + 128 up features so
+// that one 256-column tile holds matching gate and up columns. When the GEMM
+// has too few output tiles to fill the 148 SMs (decode: 32 rows), it is split
+// along K into fp32 partials and a reduce kernel applies the same epilogue.
+#include <vector>
+
+#include "decoder_epi.cuh"
+#include "gemm_launch.cuh"
+#include "kernels.h"
+
+namespace {
+
+// rstd[row] = 1 / sqrt(mean(x[row]^2) + eps); one warp per row, 16-byte loads.
+__global__ void rownorm_kernel(const uint16_t* __restrict__ x, int M, int D, float eps,
+                               float* __restrict__ rstd) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const uint4* p = reinterpret_cast<const uint4*>(x + (int64_t)row * D);
+  float acc = 0.f;
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 w = p[c];
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float a = __uint_as_float(ws[m] << 16), b = __uint_as_float(ws[m] & 0xFFFF0000u);
+      acc += a * a + b * b;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) rstd[row] = rsqrtf(acc / (float)D + eps);
+}
+
+__device__ __forceinline__ void sum_partials(const float* __restrict__ part, int ksplit, int M,
+                                             int N, int row, int col, float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  for (int k = 0; k < ksplit; ++k) {
+    const float4* p =
+        reinterpret_cast<const float4*>(part + ((int64_t)k * M + row) * N + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 t = p[j];
+      v[4 * j] += t.x;
+      v[4 * j + 1] += t.y;
+      v[4 * j + 2] += t.z;
+      v[4 * j + 3] += t.w;
+    }
+  }
+}
+
+// Split-K reductions: one thread per (row, 32-column chunk).
+__global__ void reduce_store_kernel(const float* __restrict__ part, int ksplit, int M, int N,
+                                    gemm::EpiStore e) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int chunks = N / 32;
+  if (t >= (int64_t)M * chunks) return;
+  const int row = (int)(t / chunks), col = (int)(t % chunks) * 32;
+  float v[32];
+  sum_partials(part, ksplit, M, N, row, col, v);
+  const float sc = e.row_scale ? e.row_scale[row] * e.alpha : e.alpha;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] *= sc;
+  if (e.residual) {
+    const uint16_t* r = e.residual + (int64_t)row * e.ld_res + col;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += gemm::bf16_bits_to_f32(r[j]);
+  }
+  gemm::store_row32(e.out, e.ldo, e.out_f32, row, col, e.N, v);
+}
+
+__global__ void reduce_qkv_kernel(const float* __restrict__ part, int ksplit, int M, int N,
+                                  dec::QkvParams qp) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int chunks = N / 32;
+  if (t >= (int64_t)M * chunks) return;
+  const int row = (int)(t / chunks), col = (int)(t % chunks) * 32;
+  float v[32];
+  sum_partials(part, ksplit, M, N, row, col, v);
+  qp.apply(row, col, v);
+}
+
+// N = 2*FF packed columns; thread per (row, 32 output features).
+__global__ void reduce_swiglu_kernel(const float* __restrict__ part, int ksplit, int M, int N,
+                                     dec::SwigluParams sp) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int chunks = sp.FF / 32;
+  if (t >= (int64_t)M * chunks) return;
+  const int row = (int)(t / chunks), f = (int)(t % chunks) * 32;
+  const int gcol = (f / 128) * 256 + f % 128;
+  float g[32], u[32];
+  sum_partials(part, ksplit, M, N, row, gcol, g);
+  sum_partials(part, ksplit, M, N, row, gcol + 128, u);
+  sp.apply(row, f, g, u);
+}
+
+// out[n][k] = in[k * ld_in + col_idx[n]] for k < K: packs selected columns of a
+// row-major (in, out) weight into a K-major [n, K] operand (32x32 smem tiles).
+__global__ void pack_cols_kernel(const uint16_t* __restrict__ in, int64_t ld_in, int K,
+                                 const int* __restrict__ col_idx, int Nout,
+                                 uint16_t* __restrict__ out) {
+  __shared__ uint16_t T[32][34];
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < 32; r += 8)
+    if (k0 + r < K && n0 + tx < Nout) T[r][tx] = in[(int64_t)(k0 + r) * ld_in + col_idx[n0 + tx]];
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8)
+    if (n0 + r < Nout && k0 + tx < K) out[(int64_t)(n0 + r) * K + k0 + tx] = T[tx][r];
+}
+
+}  // namespace
+
+namespace {
+
+using namespace gemm;
+
+struct Layer {
+  mb_decoder_config cfg;
+  int rank, world;
+  int Hq, Hkv, Dq, Dkv, FF;  // per-rank
+  uint16_t *wqkv, *wo, *wgu, *wdown;  // packed K-major
+};
+
+int upload_idx(const std::vector<int>& v, int** d) {
+  MB_CUDA(cudaMalloc(d, v.size() * sizeof(int)));
+  MB_CUDA(cudaMemcpy(*d, v.data(), v.size() * sizeof(int), cudaMemcpyHostToDevice));
+  return MB_OK;
+}
+
+int pack(const uint16_t* in, int64_t ld_in, int K, const std::vector<int>& cols, uint16_t** out) {
+  int* idx = nullptr;
+  int rc = upload_idx(cols, &idx);
+  if (rc) return rc;
+  const int N = (int)cols.size();
+  MB_CUDA(cudaMalloc(out, (size_t)N * K * 2));
+  dim3 g((N + 31) / 32, (K + 31) / 32);
+  pack_cols_kernel<<<g, 256>>>(in, ld_in, K, idx, N, *out);
+  MB_CUDA(cudaGetLastError());
+  MB_CUDA(cudaDeviceSynchronize());
+  MB_CUDA(cudaFree(idx));
+  return MB_OK;
+}
+
+int choose_ksplit(int64_t M, int64_t N, int64_t K) {
+  const int sms = mb::num_sms();
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  const int kb = (int)((K + 63) / 64);
+  if (tiles * 2 > sms) return 1;
+  int ks = (int)(sms / tiles);
+  if (ks > kb / 4) ks = kb / 4;  // keep at least 4 k-blocks per split
+  if (ks <= 1) return 1;
+  const int per = (kb + ks - 1) / ks;  // same normalisation as launch_gemm
+  return (kb + per - 1) / per;
+}
+
+struct Plan {
+  int64_t T;
+  int ks_qkv, ks_o, ks_gu, ks_down;
+  size_t off_rstd1, off_rstd2, off_q, off_attn, off_x1, off_act, off_part, off_attn_ws, total;
+  size_t attn_ws;
+};
+
+size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Plan make_plan(const Layer& L, int B, int S, int max_kv_len) {
+  Plan p;
+  const int D = L.cfg.d_model;
+  p.T = (int64_t)B * S;
+  const int64_t T = p.T;
+  const int Nqkv = L.Dq + 2 * L.Dkv;
+  p.ks_qkv = choose_ksplit(T, Nqkv, D);
+  p.ks_o = choose_ksplit(T, D, L.Dq);
+  p.ks_gu = choose_ksplit(T, 2 * L.FF, D);
+  p.ks_down = choose_ksplit(T, D, L.FF);
+  size_t part = 0;
+  auto upd = [&](int ks, int64_t N) {
+    if (ks > 1) part = std::max(part, (size_t)ks * T * N * 4);
+  };
+  upd(p.ks_qkv, Nqkv);
+  upd(p.ks_o, D);
+  upd(p.ks_gu, 2 * L.FF);
+  upd(p.ks_down, D);
+  p.attn_ws = S == 1 ? mb_attention_decode_workspace_bytes(B, L.Hq, L.Hkv, max_kv_len) : 0;
+  size_t o = 0;
+  p.off_rstd1 = o; o += a256(T * 4);
+  p.off_rstd2 = o; o += a256(T * 4);
+  p.off_q = o; o += a256(T * L.Dq * 2);
+  p.off_attn = o; o += a256(T * L.Dq * 2);
+  p.off_x1 = o; o += a256(T * D * 2);
+  p.off_act = o; o += a256(T * L.FF * 2);
+  p.off_part = o; o += a256(part);
+  p.off_attn_ws = o; o += a256(p.attn_ws);
+  p.total = o;
+  return p;
+}
+
+template <class Epi>
+int gemm_call(const uint16_t* A, const uint16_t* Bw, const Epi& e, int64_t M, int64_t N, int64_t K,
+              cudaStream_t s) {
+  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s);
+}
+
+int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, int64_t N,
+                 int64_t K, int ks, cudaStream_t s) {
+  dec::EpiPartial<256> e;
+  e.M = (int)M;
+  e.N = (int)N;
+  e.ws = part;
+  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s);
+}
+
+unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
+
+}  // namespace
+
+extern "C" int mb_decoder_layer_create(const mb_decoder_config* cfg, const uint16_t* W_qkv,
+                                       const uint16_t* W_o, const uint16_t* W_gu,
+                                       const uint16_t* W_down, int tp_rank, int tp_world,
+                                       void** layer) {
+  MB_REQUIRE(cfg && layer && W_qkv && W_o && W_gu && W_down, "decoder create: null argument");
+  const int D = cfg->d_model, H = cfg->n_heads, Hkv = cfg->n_kv_heads, Dh = cfg->head_dim,
+            FF = cfg->ffn;
+  MB_REQUIRE(Dh == 128, "decoder: head_dim must be 128");
+  MB_REQUIRE(H * Dh == D, "decoder: n_heads * head_dim must equal d_model");
+  MB_REQUIRE(Hkv > 0 && H % Hkv == 0, "decoder: n_heads must be a multiple of n_kv_heads");
+  MB_REQUIRE(tp_world >= 1 && tp_rank >= 0 && tp_rank < tp_world, "decoder: bad tp rank/world");
+  MB_REQUIRE(Hkv % tp_world == 0, "decoder: n_kv_heads must be divisible by the TP size");
+  MB_REQUIRE(FF % (128 * tp_world) == 0, "decoder: ffn must be a multiple of 128 * TP size");
+  MB_REQUIRE(D % 256 == 0, "decoder: d_model must be a multiple of 256");
+  Layer* L = new Layer();
+  L->cfg = *cfg;
+  L->rank = tp_rank;
+  L->world = tp_world;
+  L->Hq = H / tp_world;
+  L->Hkv = Hkv / tp_world;
+  L->Dq = L->Hq * Dh;
+  L->Dkv = L->Hkv * Dh;
+  L->FF = FF / tp_world;
+  const int Ntot = D + 2 * Hkv * Dh;
+  std::vector<int> cols;
+  for (int c = 0; c < L->Dq; ++c) cols.push_back(tp_rank * L->Dq + c);
+  for (int c = 0; c < L->Dkv; ++c) cols.push_back(D + tp_rank * L->Dkv + c);
+  for (int c = 0; c < L->Dkv; ++c) cols.push_back(D + Hkv * Dh + tp_rank * L->Dkv + c);
+  int rc = pack(W_qkv, Ntot, D, cols, &L->wqkv);
+  std::vector<int> ident(D);
+  for (int c = 0; c < D; ++c) ident[c] = c;
+  if (!rc) rc = pack(W_o + (int64_t)tp_rank * L->Dq * D, D, L->Dq, ident, &L->wo);
+  std::vector<int> gu;
+  for (int p = 0; p < 2 * L->FF; ++p) {
+    const int t = p / 256, w = p % 256;
+    const int f = tp_rank * L->FF + t * 128 + (w % 128);
+    gu.push_back(w < 128 ? f : FF + f);
+  }
+  if (!rc) rc = pack(W_gu, 2 * FF, D, gu, &L->wgu);
+  if (!rc) rc = pack(W_down + (int64_t)tp_rank * L->FF * D, D, L->FF, ident, &L->wdown);
+  if (rc) {
+    delete L;
+    return rc;
+  }
+  *layer = L;
+  return MB_OK;
+}
+
+extern "C" void mb_decoder_layer_destroy(void* layer) {
+  Layer* L = static_cast<Layer*>(layer);
+  if (!L) return;
+  cudaFree(L->wqkv);
+  cudaFree(L->wo);
+  cudaFree(L->wgu);
+  cudaFree(L->wdown);
+  delete L;
+}
+
+extern "C" size_t mb_decoder_layer_workspace_bytes(const void* layer, int B, int S,
+                                                   int max_kv_len) {
+  if (!layer || B <= 0 || S <= 0) return 0;
+  return make_plan(*static_cast<const Layer*>(layer), B, S, max_kv_len).total;
+}
+
+extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, int B,
+                                        int S, const int* start_pos, const int* kv_len,
+                                        int max_kv_len, uint16_t* k_cache, uint16_t* v_cache,
+                                        const int* block_table, int max_pages, int causal,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  MB_REQUIRE(layer && x && y && start_pos && kv_len && k_cache && v_cache && block_table,
+             "decoder forward: null argument");
+  MB_REQUIRE(B >= 0 && S >= 0, "decoder forward: negative size");
+  if (B == 0 || S == 0) return MB_OK;
+  const Layer& L = *static_cast<const Layer*>(layer);
+  MB_REQUIRE(max_kv_len >= S && max_kv_len <= max_pages * 64,
+             "decoder forward: max_kv_len must be in [S, max_pages*64]");
+  const Plan p = make_plan(L, B, S, max_kv_len);
+  MB_REQUIRE(workspace && workspace_bytes >= p.total &&
+                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "decoder forward: workspace of %zu bytes (256-byte aligned) required", p.total);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  float* rstd1 = reinterpret_cast<float*>(w + p.off_rstd1);
+  float* rstd2 = reinterpret_cast<float*>(w + p.off_rstd2);
+  uint16_t* q = reinterpret_cast<uint16_t*>(w + p.off_q);
+  uint16_t* attn = reinterpret_cast<uint16_t*>(w + p.off_attn);
+  uint16_t* x1 = reinterpret_cast<uint16_t*>(w + p.off_x1);
+  uint16_t* act = reinterpret_cast<uint16_t*>(w + p.off_act);
+  float* part = reinterpret_cast<float*>(w + p.off_part);
+  const int D = L.cfg.d_model, Dh = L.cfg.head_dim;
+  const int64_t T = p.T;
+  const int Nqkv = L.Dq + 2 * L.Dkv;
+  int rc;
+
+  // 1. rstd1
+  rownorm_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(x, (int)T, D, L.cfg.eps, rstd1);
+  MB_CUDA(cudaGetLastError());
+
+  // 2. QKV + RoPE + KV-cache write
+  dec::QkvParams qp;
+  qp.M = (int)T;
+  qp.S = S;
+  qp.Hq = L.Hq;
+  qp.Hkv = L.Hkv;
+  qp.Dh = Dh;
+  qp.neg_log2_base_over_half = -log2f(L.cfg.rope_base) / (float)(Dh / 2);
+  qp.rstd = rstd1;
+  qp.start_pos = start_pos;
+  qp.q_out = q;
+  qp.kv = dec::KvCache{k_cache, v_cache, block_table, max_pages, 64};
+  if (p.ks_qkv > 1) {
+    rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s);
+    if (rc) return rc;
+    reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, p.ks_qkv, (int)T, Nqkv, qp);
+  } else {
+    dec::EpiQKV<256> e;
+    e.M = (int)T;
+    e.N = Nqkv;
+    e.q = qp;
+    rc = gemm_call(x, L.wqkv, e, T, Nqkv, D, s);
+    if (rc) return rc;
+  }
+  MB_CUDA(cudaGetLastError());
+
+  // 3. attention
+  if (S == 1)
+    rc = mb_attention_decode_bf16(q, L.Dq, k_cache, v_cache, block_table, max_pages, kv_len,
+                                  max_kv_len, B, L.Hq, L.Hkv, Dh, attn, L.Dq, w + p.off_attn_ws,
+                                  p.attn_ws, s);
+  else
+    rc = mb_attention_prefill_bf16(q, L.Dq, k_cache, v_cache, block_table, max_pages, start_pos,
+                                   kv_len, B, S, L.Hq, L.Hkv, Dh, causal, attn, L.Dq, s);
+  if (rc) return rc;
+
+  // 4. x1 = x + attn @ Wo (rank 0 adds the residual; the all-reduce sums shards)
+  EpiStore eo{};
+  eo.M = (int)T;
+  eo.N = D;
+  eo.out = x1;
+  eo.ldo = D;
+  eo.alpha = 1.f;
+  eo.residual = L.rank == 0 ? x : nullptr;
+  eo.ld_res = D;
+  if (p.ks_o > 1) {
+    rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s);
+    if (rc) return rc;
+    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, p.ks_o, (int)T, D, eo);
+  } else {
+    Epi<256, EpiStore> e{};
+    static_cast<EpiStore&>(e) = eo;
+    rc = gemm_call(attn, L.wo, e, T, D, L.Dq, s);
+    if (rc) return rc;
+  }
+  MB_CUDA(cudaGetLastError());
+  if (L.world > 1) {
+    rc = mb::tp_allreduce_bf16(x1, (size_t)T * D, s);
+    if (rc) return rc;
+  }
+
+  // 5. rstd2, 6. SwiGLU MLP up
+  rownorm_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(x1, (int)T, D, L.cfg.eps, rstd2);
+  MB_CUDA(cudaGetLastError());
+  dec::SwigluParams sp;
+  sp.M = (int)T;
+  sp.FF = L.FF;
+  sp.rstd = rstd2;
+  sp.act = act;
+  if (p.ks_gu > 1) {
+    rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s);
+    if (rc) return rc;
+    reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, p.ks_gu, (int)T,
+                                                                    2 * L.FF, sp);
+  } else {
+    dec::EpiSwiGLU e;
+    e.M = (int)T;
+    e.p = sp;
+    rc = gemm_call(x1, L.wgu, e, T, 2 * L.FF, D, s);
+    if (rc) return rc;
+  }
+  MB_CUDA(cudaGetLastError());
+
+  // 7. y = x1 + act @ Wdown
+  EpiStore ed{};
+  ed.M = (int)T;
+  ed.N = D;
+  ed.out = y;
+  ed.ldo = D;
+  ed.alpha = 1.f;
+  ed.residual = L.rank == 0 ? x1 : nullptr;
+  ed.ld_res = D;
+  if (p.ks_down > 1) {
+    rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s);
+    if (rc) return rc;
+    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, p.ks_down, (int)T, D, ed);
+  } else {
+    Epi<256, EpiStore> e{};
+    static_cast<EpiStore&>(e) = ed;
+    rc = gemm_call(act, L.wdown, e, T, D, L.FF, s);
+    if (rc) return rc;
+  }
+  MB_CUDA(cudaGetLastError());
+  if (L.world > 1) {
+    rc = mb::tp_allreduce_bf16(y, (size_t)T * D, s);
+    if (rc) return rc;
+  }
+  return MB_OK;
+}

@@ -65,6 +65,27 @@ __device__ __forceinline__ void store_row32(void* out, int64_t ldo, int out_f32,
   }
 }
 
+// 32 bf16 values to p (vectorised when 16-byte aligned).
+__device__ __forceinline__ void store32_bf16(uint16_t* p, const float (&v)[32]) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 w;
+      w.x = pack_bf16(v[j], v[j + 1]);
+      w.y = pack_bf16(v[j + 2], v[j + 3]);
+      w.z = pack_bf16(v[j + 4], v[j + 5]);
+      w.w = pack_bf16(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4*>(p + j) = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+      p[j] = *reinterpret_cast<uint16_t*>(&h);
+    }
+  }
+}
+
 // out[row, n] = alpha * row_scale[row] * acc[row, n] (+ residual[row, n]),
 // stored as bf16 or fp32. row_scale and residual are optional (null).
 struct EpiStore {

@@ -1,0 +1,51 @@
+// Host-side launcher for the tcgen05 GEMM core with 2-D tensor-map operands.
+#pragma once
+#include "gemm_core.cuh"
+
+namespace gemm {
+
+template <Mode MODE, int BN, int STAGES, bool B_MN, class Epi>
+inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, int64_t N, int64_t K,
+                int ksplit, cudaStream_t stream) {
+  using S = Smem<MODE, BN, STAGES>;
+  using P = GemmProducer<MODE, BN, B_MN>;
+  const int esz = elem_bytes(MODE);
+  const CUtensorMapDataType dt =
+      MODE == Mode::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  MB_REQUIRE((K * esz) % 16 == 0, "gemm: K*elem_size must be a multiple of 16 bytes (K=%lld)",
+             (long long)K);
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(B) % 16 == 0,
+             "gemm: operands must be 16-byte aligned");
+  MB_REQUIRE(!B_MN || (N * esz) % 16 == 0, "gemm: N*elem_size must be a multiple of 16 bytes");
+  P p;
+  int rc = mb::make_tmap_2d(&p.a, A, dt, esz, K, M, K * esz, P::KE, BM,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (!B_MN)
+    rc = mb::make_tmap_2d(&p.b, B, dt, esz, K, N, K * esz, P::KE, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    rc = mb::make_tmap_2d(&p.b, B, dt, esz, N, K, N * esz, P::KE, P::KE,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  Sched sc;
+  sc.tiles_m = (int)((M + BM - 1) / BM);
+  sc.tiles_n = (int)((N + BN - 1) / BN);
+  sc.kblocks = (int)((K + P::KE - 1) / P::KE);
+  sc.ksplit = ksplit < 1 ? 1 : (ksplit > sc.kblocks ? sc.kblocks : ksplit);
+  sc.kb_per_split = (sc.kblocks + sc.ksplit - 1) / sc.ksplit;
+  // no empty trailing split: every split owns at least one k-block
+  sc.ksplit = (sc.kblocks + sc.kb_per_split - 1) / sc.kb_per_split;
+  auto kern = gemm_kernel<MODE, BN, STAGES, B_MN, P, Epi>;
+  static bool attr = false;  // one instantiation = one static
+  if (!attr) {
+    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr = true;
+  }
+  const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
+  kern<<<grid, num_warps(MODE) * 32, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+
+}  // namespace gemm

@@ -58,5 +58,7 @@ void register_all_kernels();  // defined in registry.cu
 // tensor parallel communicator (tp.cu)
 int tp_init(int rank, int world, const char* nccl_id_path, int timeout_ms);
 void tp_shutdown();
+int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream);
+int tp_world();
 
 }  // namespace mb
