@@ -10,10 +10,11 @@
 // Cache layout (both kernels): k, v = [num_pages][Hkv][PAGE=64][Dh=128] bf16,
 // sequence b's position p in page block_table[b*max_pages + p/64], slot p%64.
 //
-//  * decode: one new token per sequence. Memory-bound split-KV kernel on CUDA
-//    cores: a CTA owns (sequence, kv head, key split) and ALL G query heads of
-//    that kv head, so every K/V byte is read once; partial (max, sum, o)
-//    triples are merged by a small combine kernel.
+//  * decode: one new token per sequence. Memory-bound split-KV kernel: a CTA
+//    owns (sequence, kv head, key split) and ALL G query heads of that kv
+//    head (the 16 rows of a warp MMA), so every K/V byte is read once; whole
+//    16 KiB pages stream into shared memory through a cp.async ring; partial
+//    (max, sum, o) triples are merged by a small combine kernel.
 //  * prefill: FlashAttention-2 style tiles on the warp-level bf16 tensor-core
 //    MMA (mma.sync m16n8k16), 64 queries x 64 keys per step, online softmax in
 //    fp32, causal skip of key tiles above the diagonal.
@@ -27,134 +28,6 @@ constexpr int DH = 128;
 __device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 __device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-
-// ---------------------------------------------------------------------------
-// decode
-// ---------------------------------------------------------------------------
-// grid (splits, Hkv, B), 128 threads (4 warps). Each warp walks 32 keys at a
-// time: lane = key for q.k (the key's 256-byte row read by its lane, q for the
-// G heads broadcast from shared memory), then lane = 4 dims for p.v.
-template <int G>
-__global__ void __launch_bounds__(128) attn_decode_kernel(
-    const uint16_t* __restrict__ q, int ldq, const uint16_t* __restrict__ kc,
-    const uint16_t* __restrict__ vc, const int* __restrict__ block_table, int max_pages,
-    const int* __restrict__ kv_len, int Hkv, int keys_per_split, float scale_log2,
-    float* __restrict__ part_o, float* __restrict__ part_ml) {
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int splits = gridDim.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ __align__(16) float qs[G][DH];
-  __shared__ float wm[4][G], wl[4][G];
-  __shared__ __align__(16) float wo[4][G][DH];
-
-  for (int i = threadIdx.x; i < G * DH; i += 128) {
-    const int g = i / DH, d = i % DH;
-    qs[g][d] = bf2f(q[(int64_t)b * ldq + (kvh * G + g) * DH + d]);
-  }
-  __syncthreads();
-
-  const int L = kv_len[b];
-  const int k_begin = split * keys_per_split;
-  const int k_end = min(L, k_begin + keys_per_split);
-  float m[G], l[G], o[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[g][j] = 0.f;
-  }
-  for (int k0 = k_begin + warp * 32; k0 < k_end; k0 += 128) {
-    const int key = k0 + lane;
-    const bool valid = key < k_end;
-    float s[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = 0.f;
-    const int kk = valid ? key : k0;
-    const int pg = block_table[b * max_pages + kk / PAGE];
-    const int64_t row = (((int64_t)pg * Hkv + kvh) * PAGE + kk % PAGE) * DH;
-    const uint4* kr = reinterpret_cast<const uint4*>(kc + row);
-#pragma unroll 4
-    for (int c = 0; c < DH / 8; ++c) {
-      const uint4 w = kr[c];
-      const float kf[8] = {lo_bf(w.x), hi_bf(w.x), lo_bf(w.y), hi_bf(w.y),
-                           lo_bf(w.z), hi_bf(w.z), lo_bf(w.w), hi_bf(w.w)};
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 qa = *reinterpret_cast<const float4*>(&qs[g][c * 8]);
-        const float4 qb = *reinterpret_cast<const float4*>(&qs[g][c * 8 + 4]);
-        s[g] += qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] +
-                qb.y * kf[5] + qb.z * kf[6] + qb.w * kf[7];
-      }
-    }
-    // online softmax over this group of 32 keys (log2 domain)
-    float p[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float sv = valid ? s[g] * scale_log2 : -INFINITY;
-      float mx = sv;
-#pragma unroll
-      for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mn = fmaxf(m[g], mx);
-      const float corr = exp2f(m[g] - mn);  // m = -inf initially -> 0
-      p[g] = valid ? exp2f(sv - mn) : 0.f;
-      float ps = p[g];
-#pragma unroll
-      for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-      l[g] = l[g] * corr + ps;
-      m[g] = mn;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[g][j] *= corr;
-    }
-    // p . v: lane owns dims 4*lane..4*lane+3, loops over the 32 keys
-    const int nk = min(32, k_end - k0);
-    for (int t = 0; t < nk; ++t) {
-      const int key2 = k0 + t;
-      const int pg2 = block_table[b * max_pages + key2 / PAGE];
-      const int64_t row2 = (((int64_t)pg2 * Hkv + kvh) * PAGE + key2 % PAGE) * DH;
-      const uint2 w = *reinterpret_cast<const uint2*>(vc + row2 + 4 * lane);
-      const float v0 = lo_bf(w.x), v1 = hi_bf(w.x), v2 = lo_bf(w.y), v3 = hi_bf(w.y);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float pt = __shfl_sync(0xffffffffu, p[g], t);
-        o[g][0] += pt * v0;
-        o[g][1] += pt * v1;
-        o[g][2] += pt * v2;
-        o[g][3] += pt * v3;
-      }
-    }
-  }
-  // merge the 4 warps of the CTA
-  if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      wm[warp][g] = m[g];
-      wl[warp][g] = l[g];
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    *reinterpret_cast<float4*>(&wo[warp][g][4 * lane]) =
-        make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-  __syncthreads();
-  const int64_t unit = ((int64_t)b * Hkv + kvh) * splits + split;
-  for (int i = threadIdx.x; i < G * DH; i += 128) {
-    const int g = i / DH, d = i % DH;
-    float M = -INFINITY;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][g]);
-    float Ls = 0.f, acc = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      const float c = wm[w][g] == -INFINITY ? 0.f : exp2f(wm[w][g] - M);
-      Ls += wl[w][g] * c;
-      acc += wo[w][g][d] * c;
-    }
-    part_o[(unit * G + g) * DH + d] = acc;
-    if (d == 0) {
-      part_ml[(unit * G + g) * 2] = M;
-      part_ml[(unit * G + g) * 2 + 1] = Ls;
-    }
-  }
-}
 
 // out[b, (kvh*G+g)*DH + d] = sum_split o * 2^(m - M) / sum_split l * 2^(m - M)
 __global__ void attn_combine_kernel(const float* __restrict__ part_o,
@@ -383,22 +256,206 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(
 }  // namespace
 
 namespace {
-int decode_splits(int B, int Hkv, int max_kv_len, int* keys_per_split) {
-  // Aim for about 4 CTAs per SM; splits are whole multiples of 128 keys.
-  const int units = B * Hkv;
-  int want = (4 * mb::num_sms() + units - 1) / units;
-  int kps = (max_kv_len + want - 1) / want;
-  kps = ((kps + 127) / 128) * 128;
-  if (kps < 128) kps = 128;
-  *keys_per_split = kps;
-  return (max_kv_len + kps - 1) / kps;
+
+// ---------------------------------------------------------------------------
+// decode on the warp MMA: the G query heads of one kv head are the 16 MMA rows
+// (rows >= G are zero). grid (splits, Hkv, B), 128 threads. Pages of the
+// split's key range are staged whole (K and V, 16 KiB each) into a
+// three-deep cp.async ring; warp w takes keys 16w..16w+15 of every page and
+// keeps its own online-softmax state; the four warps are merged at the end and
+// one (max, sum, o) partial per split goes to the combine kernel.
+// ---------------------------------------------------------------------------
+constexpr int DEC_STAGES = 3;
+
+__global__ void __launch_bounds__(128) attn_decode_mma_kernel(
+    const uint16_t* __restrict__ q, int ldq, const uint16_t* __restrict__ kc,
+    const uint16_t* __restrict__ vc, const int* __restrict__ block_table, int max_pages,
+    const int* __restrict__ kv_len, int Hkv, int G, int pages_per_split, float scale_log2,
+    float* __restrict__ part_o, float* __restrict__ part_ml) {
+  extern __shared__ __align__(16) uint16_t sm[];
+  uint16_t* Ks = sm;                                // [STAGES][64][KV_LD]
+  uint16_t* Vs = sm + DEC_STAGES * PAGE * KV_LD;    // [STAGES][64][KV_LD]
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, splits = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int L = kv_len[b];
+  const int pg_begin = split * pages_per_split;
+  const int pg_end = min((L + PAGE - 1) / PAGE, pg_begin + pages_per_split);
+  const int npg = max(0, pg_end - pg_begin);
+
+  uint32_t qa[8][4];
+  {
+    const uint16_t* qr = q + (int64_t)b * ldq + (kvh * G) * DH;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int c = ks * 16 + tig * 2;
+      const bool ra = gid < G, rb = gid + 8 < G;
+      qa[ks][0] = ra ? *reinterpret_cast<const uint32_t*>(qr + gid * DH + c) : 0u;
+      qa[ks][1] = rb ? *reinterpret_cast<const uint32_t*>(qr + (gid + 8) * DH + c) : 0u;
+      qa[ks][2] = ra ? *reinterpret_cast<const uint32_t*>(qr + gid * DH + c + 8) : 0u;
+      qa[ks][3] = rb ? *reinterpret_cast<const uint32_t*>(qr + (gid + 8) * DH + c + 8) : 0u;
+    }
+  }
+  auto load_page = [&](int i, int buf) {
+    const int kt = pg_begin + i;
+    const int pg = block_table[b * max_pages + kt];
+    const int64_t base = ((int64_t)pg * Hkv + kvh) * PAGE * DH;
+    for (int c = threadIdx.x; c < PAGE * DH / 8; c += 128) {
+      const int row = c >> 4, col = (c & 15) * 8;
+      const bool ok = kt * PAGE + row < L;
+      cp_async16(Ks + (buf * PAGE + row) * KV_LD + col, kc + base + row * DH + col, ok);
+      cp_async16(Vs + (buf * PAGE + row) * KV_LD + col, vc + base + row * DH + col, ok);
+    }
+  };
+  // prologue: STAGES-1 pages in flight (empty groups keep the counting uniform)
+#pragma unroll
+  for (int i = 0; i < DEC_STAGES - 1; ++i) {
+    if (i < npg) load_page(i, i);
+    cp_async_commit();
+  }
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+
+  for (int i = 0; i < npg; ++i) {
+    const int buf = i % DEC_STAGES;
+    if (i + DEC_STAGES - 1 < npg) load_page(i + DEC_STAGES - 1, (i + DEC_STAGES - 1) % DEC_STAGES);
+    cp_async_commit();
+    cp_async_wait<DEC_STAGES - 1>();
+    __syncthreads();
+    const uint16_t* K = Ks + (buf * PAGE + warp * 16) * KV_LD;
+    const uint16_t* V = Vs + (buf * PAGE + warp * 16) * KV_LD;
+    const int key0 = (pg_begin + i) * PAGE + warp * 16;
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const uint16_t* kr = K + (nt * 8 + gid) * KV_LD + tig * 2;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        mma_bf16_16816(s[nt], qa[ks], *reinterpret_cast<const uint32_t*>(kr + ks * 16),
+                       *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8));
+    }
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool ok = key0 + nt * 8 + tig * 2 + e < L;
+        s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
+        s[nt][2 + e] = ok ? s[nt][2 + e] * scale_log2 : -INFINITY;
+        mx_a = fmaxf(mx_a, s[nt][e]);
+        mx_b = fmaxf(mx_b, s[nt][2 + e]);
+      }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+    }
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    const float sa = mn_a == -INFINITY ? 0.f : mn_a, sb = mn_b == -INFINITY ? 0.f : mn_b;
+    const float ca = exp2f(m_a - sa), cb = exp2f(m_b - sb);
+    m_a = mn_a;
+    m_b = mn_b;
+    float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - sa);
+      s[nt][1] = exp2f(s[nt][1] - sa);
+      s[nt][2] = exp2f(s[nt][2] - sb);
+      s[nt][3] = exp2f(s[nt][3] - sb);
+      sum_a += s[nt][0] + s[nt][1];
+      sum_b += s[nt][2] + s[nt][3];
+    }
+    l_a = l_a * ca + sum_a;
+    l_b = l_b * cb + sum_b;
+    uint32_t pa[4];
+    pa[0] = pack2(s[0][0], s[0][1]);
+    pa[1] = pack2(s[0][2], s[0][3]);
+    pa[2] = pack2(s[1][0], s[1][1]);
+    pa[3] = pack2(s[1][2], s[1][3]);
+    const uint16_t* v0 = V + (tig * 2) * KV_LD + gid;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      o[dt][0] *= ca;
+      o[dt][1] *= ca;
+      o[dt][2] *= cb;
+      o[dt][3] *= cb;
+      const uint16_t* vp = v0 + dt * 8;
+      const uint32_t b0 = (uint32_t)vp[0] | ((uint32_t)vp[KV_LD] << 16);
+      const uint32_t b1 = (uint32_t)vp[8 * KV_LD] | ((uint32_t)vp[9 * KV_LD] << 16);
+      mma_bf16_16816(o[dt], pa, b0, b1);
+    }
+    __syncthreads();  // this buffer is refilled STAGES-1 iterations later
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // the ring is reused below as the merge area
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+  }
+  // merge warps: [4 warps][16 rows] m, l then [4][16][DH] o (33 KB < ring)
+  float* red = reinterpret_cast<float*>(sm);
+  float* rm = red;
+  float* rl = red + 64;
+  float* ro = red + 128;
+  if (tig == 0) {
+    rm[warp * 16 + gid] = m_a;
+    rm[warp * 16 + gid + 8] = m_b;
+    rl[warp * 16 + gid] = l_a;
+    rl[warp * 16 + gid + 8] = l_b;
+  }
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt) {
+    const int d = dt * 8 + tig * 2;
+    ro[(warp * 16 + gid) * DH + d] = o[dt][0];
+    ro[(warp * 16 + gid) * DH + d + 1] = o[dt][1];
+    ro[(warp * 16 + gid + 8) * DH + d] = o[dt][2];
+    ro[(warp * 16 + gid + 8) * DH + d + 1] = o[dt][3];
+  }
+  __syncthreads();
+  const int64_t unit = ((int64_t)b * Hkv + kvh) * splits + split;
+  for (int idx = threadIdx.x; idx < G * DH; idx += 128) {
+    const int g = idx / DH, d = idx % DH;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, rm[w * 16 + g]);
+    float Ls = 0.f, acc = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float mw = rm[w * 16 + g];
+      const float c = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      Ls += rl[w * 16 + g] * c;
+      acc += ro[(w * 16 + g) * DH + d] * c;
+    }
+    part_o[(unit * G + g) * DH + d] = acc;
+    if (d == 0) {
+      part_ml[(unit * G + g) * 2] = M;
+      part_ml[(unit * G + g) * 2 + 1] = Ls;
+    }
+  }
 }
+
+}  // namespace
+
+namespace {
+// Pages per split: aim for about two CTAs per SM over all (sequence, kv head).
+int decode_split_pages(int B, int Hkv, int max_kv_len, int* splits) {
+  const int units = B * Hkv;
+  const int pages = (max_kv_len + PAGE - 1) / PAGE;
+  const int want = (2 * mb::num_sms() + units - 1) / units;
+  int pps = (pages + want - 1) / want;
+  if (pps < 1) pps = 1;
+  *splits = (pages + pps - 1) / pps;
+  return pps;
+}
+constexpr int DEC_SMEM = 2 * DEC_STAGES * PAGE * KV_LD * 2;
 }  // namespace
 
 extern "C" size_t mb_attention_decode_workspace_bytes(int B, int Hq, int Hkv, int max_kv_len) {
   if (B <= 0 || Hkv <= 0 || max_kv_len <= 0) return 0;
-  int kps;
-  const int splits = decode_splits(B, Hkv, max_kv_len, &kps);
+  int splits;
+  decode_split_pages(B, Hkv, max_kv_len, &splits);
   const size_t units = (size_t)B * Hq * splits;
   return units * DH * 4 + units * 2 * 4 + 256;
 }
@@ -411,29 +468,27 @@ extern "C" int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16
   MB_REQUIRE(Dh == DH, "attention: head_dim must be 128 (got %d)", Dh);
   MB_REQUIRE(Hkv > 0 && Hq % Hkv == 0, "attention: Hq must be a multiple of Hkv");
   const int G = Hq / Hkv;
-  MB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "attention decode: G = Hq/Hkv must be 1, 2, 4 or 8");
+  MB_REQUIRE(G <= 16, "attention decode: at most 16 query heads per kv head");
   MB_REQUIRE(max_kv_len > 0 && max_kv_len <= max_pages * PAGE, "attention: bad max_kv_len");
   if (B == 0) return MB_OK;
   const size_t need = mb_attention_decode_workspace_bytes(B, Hq, Hkv, max_kv_len);
   MB_REQUIRE(workspace && workspace_bytes >= need,
              "attention decode: workspace of %zu bytes required", need);
-  int kps;
-  const int splits = decode_splits(B, Hkv, max_kv_len, &kps);
+  int splits;
+  const int pps = decode_split_pages(B, Hkv, max_kv_len, &splits);
   float* part_o = static_cast<float*>(workspace);
   float* part_ml = part_o + (size_t)B * Hq * splits * DH;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)DH);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 grid(splits, Hkv, B);
-#define MB_DEC(GG)                                                                               \
-  attn_decode_kernel<GG><<<grid, 128, 0, s>>>(q, ldq, k_cache, v_cache, block_table, max_pages, \
-                                              kv_len, Hkv, kps, scale_log2, part_o, part_ml)
-  switch (G) {
-    case 1: MB_DEC(1); break;
-    case 2: MB_DEC(2); break;
-    case 4: MB_DEC(4); break;
-    default: MB_DEC(8); break;
+  static bool attr = false;
+  if (!attr) {
+    MB_CUDA(cudaFuncSetAttribute(attn_decode_mma_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM));
+    attr = true;
   }
-#undef MB_DEC
+  attn_decode_mma_kernel<<<dim3(splits, Hkv, B), 128, DEC_SMEM, s>>>(
+      q, ldq, k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, pps, scale_log2, part_o,
+      part_ml);
   MB_CUDA(cudaGetLastError());
   attn_combine_kernel<<<dim3(G, Hkv, B), DH, 0, s>>>(part_o, part_ml, splits, G, Hkv, out, ldo);
   MB_CUDA(cudaGetLastError());
@@ -473,3 +528,4 @@ extern "C" int mb_attention_prefill_bf16(const uint16_t* q, int ldq, const uint1
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
+

@@ -69,7 +69,23 @@ __device__ __forceinline__ void sum_partials(const float* __restrict__ part, int
   }
 }
 
-// Split-K reductions: one thread per (row, 32-column chunk).
+// part[0] += part[1..ksplit-1], four floats per thread (wide, so the sum is
+// bandwidth- not latency-bound); the epilogue kernels then read part[0] only.
+__global__ void reduce_sum_kernel(float4* __restrict__ part, int ksplit, int64_t n4) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 a = part[i];
+  for (int k = 1; k < ksplit; ++k) {
+    const float4 t = part[k * n4 + i];
+    a.x += t.x;
+    a.y += t.y;
+    a.z += t.z;
+    a.w += t.w;
+  }
+  part[i] = a;
+}
+
+// Split-K epilogues: one thread per (row, 32-column chunk) of the summed part[0].
 __global__ void reduce_store_kernel(const float* __restrict__ part, int ksplit, int M, int N,
                                     gemm::EpiStore e) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -232,6 +248,13 @@ int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, 
 
 unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
 
+int sum_splits(float* part, int ks, int64_t M, int64_t N, cudaStream_t s) {
+  const int64_t n4 = M * N / 4;
+  reduce_sum_kernel<<<blocks_for(n4), 256, 0, s>>>(reinterpret_cast<float4*>(part), ks, n4);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
 }  // namespace
 
 extern "C" int mb_decoder_layer_create(const mb_decoder_config* cfg, const uint16_t* W_qkv,
@@ -346,8 +369,9 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   qp.kv = dec::KvCache{k_cache, v_cache, block_table, max_pages, 64};
   if (p.ks_qkv > 1) {
     rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s);
+    if (!rc) rc = sum_splits(part, p.ks_qkv, T, Nqkv, s);
     if (rc) return rc;
-    reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, p.ks_qkv, (int)T, Nqkv, qp);
+    reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, 1, (int)T, Nqkv, qp);
   } else {
     dec::EpiQKV<256> e;
     e.M = (int)T;
@@ -379,8 +403,9 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   eo.ld_res = D;
   if (p.ks_o > 1) {
     rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s);
+    if (!rc) rc = sum_splits(part, p.ks_o, T, D, s);
     if (rc) return rc;
-    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, p.ks_o, (int)T, D, eo);
+    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, 1, (int)T, D, eo);
   } else {
     Epi<256, EpiStore> e{};
     static_cast<EpiStore&>(e) = eo;
@@ -403,9 +428,10 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   sp.act = act;
   if (p.ks_gu > 1) {
     rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s);
+    if (!rc) rc = sum_splits(part, p.ks_gu, T, 2 * L.FF, s);
     if (rc) return rc;
-    reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, p.ks_gu, (int)T,
-                                                                    2 * L.FF, sp);
+    reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, 1, (int)T, 2 * L.FF,
+                                                                    sp);
   } else {
     dec::EpiSwiGLU e;
     e.M = (int)T;
@@ -426,8 +452,9 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   ed.ld_res = D;
   if (p.ks_down > 1) {
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s);
+    if (!rc) rc = sum_splits(part, p.ks_down, T, D, s);
     if (rc) return rc;
-    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, p.ks_down, (int)T, D, ed);
+    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, 1, (int)T, D, ed);
   } else {
     Epi<256, EpiStore> e{};
     static_cast<EpiStore&>(e) = ed;
