@@ -126,7 +126,13 @@ class Workload:
     unit = ""
     dtype = ""
     bound = "hbm"
+    scaling = "weak"
     config: dict = {}
+
+    def job_units(self, world: int) -> float:
+        """Whole-job metric numerator per step: weak scaling adds every rank's
+        work, strong scaling splits one job across the ranks."""
+        return self.work_per_step() * (world if self.scaling == "weak" else 1)
 
     def setup(self, torch, rank, world): ...
     def step(self): ...                  # one step on the current stream
@@ -153,7 +159,7 @@ class TransposeF32(Workload):
                        "l2": "inputs larger than L2 (256 MiB in, 256 MiB out)",
                        "parallelism": "replicas (one independent matrix per GPU)"}
 
-    def setup(self, torch, rank, world):
+    def setup(self, torch, rank, world, local):
         from metalbench_b200 import ops
         self.torch, self.ops = torch, ops
         g = torch.Generator(device="cuda").manual_seed(1 + rank)
@@ -204,8 +210,138 @@ class TransposeF32(Workload):
                                               f"512-row blocks over {threads} threads"
 
 
-WORKLOADS = {"transpose": TransposeF32}
-DEFAULT_WORKLOAD = "transpose"
+class DecoderStackDecode(Workload):
+    """8-layer LLaMA decoder stack: d_model 8192, 64 query /
+    8 kv heads, head_dim 128, SwiGLU FFN 28672, RMSNorm eps 1e-5, RoPE theta 5e5,
+    weights N(0, 0.02) seed 4; decode batch 64 at KV length 8192, tensor-parallel
+    over the GPUs. One step = one new token for each of the 64 sequences through
+    all 8 layers (a CUDA-graph replay). Every step writes its token at position
+    8192 and attends over 8193 keys, so all steps cost the same."""
+    name = "decoder_stack_decode"
+    metric = "8-layer LLaMA decoder decode throughput (tokens/s)"
+    unit = "tok/s"
+    dtype = "bf16"
+    bound = "hbm"
+    scaling = "strong"
+    default_steps = 100
+    B, L, LAYERS = 64, 8192, 8
+    D, H, HKV, FF = 8192, 64, 8, 28672
+
+    def __init__(self):
+        self.config = {"workload": "decoder_stack_decode", "model": "llama-8layer-d8192",
+                       "d_model": self.D, "n_heads": self.H, "n_kv_heads": self.HKV,
+                       "head_dim": 128, "ffn": self.FF, "layers": self.LAYERS,
+                       "global_batch": self.B, "kv_len": self.L, "rope_theta": 500000.0,
+                       "weights": "N(0,0.02) seed 4, random init", "kv_cache": "N(0,1) fill",
+                       "l2": "inputs larger than L2 (17 GB KV + 13.7 GB weights per step at 1 GPU)"}
+
+    def setup(self, torch, rank, world, local):
+        from metalbench_b200.decoder import DecoderConfig
+        from metalbench_b200.stack import DecoderStack, init_tensor_parallel
+        self.torch = torch
+        self.config["parallelism"] = f"tp{world}"
+        init_tensor_parallel(rank, world, local)
+        cfg = DecoderConfig(self.D, self.H, self.HKV, self.FF, rope_base=500000.0)
+        self.stack = DecoderStack(cfg, self.LAYERS, self.B, self.L + 64, tp_rank=rank,
+                                  tp_world=world)
+        self.stack.fill_cache_random(self.L)
+        g = torch.Generator(device="cuda").manual_seed(4)
+        self.x = torch.randn((self.B, 1, self.D), generator=g, device="cuda").bfloat16()
+        self.sp = torch.full((self.B,), self.L, dtype=torch.int32, device="cuda")
+        self.stack.capture_decode(self.x, self.sp, self.L + 1)
+        self.h_x = torch.empty((self.B, 1, self.D), dtype=torch.bfloat16, pin_memory=True)
+        self.h_x.copy_(self.x.cpu())
+        self.h_y = torch.empty((self.B, 1, self.D), dtype=torch.bfloat16, pin_memory=True)
+        # dominant kernel: decode attention of one layer, driven directly
+        from metalbench_b200 import _lib, ops
+        self._lib, self._ops = _lib, ops
+        c = self.stack.caches[0]
+        self.hq, self.hkv = self.H // world, self.HKV // world
+        self.q = torch.randn((self.B, self.hq * 128), device="cuda").bfloat16()
+        self.ao = torch.empty_like(self.q)
+        self.kvl = self.sp + 1
+        self.aws_bytes = _lib.lib().mb_attention_decode_workspace_bytes(self.B, self.hq,
+                                                                         self.hkv, self.L + 1)
+        self.aws = torch.empty(self.aws_bytes, dtype=torch.uint8, device="cuda")
+        self.cache0 = c
+
+    def step(self):
+        self.stack.replay()
+
+    def launch_dominant(self):
+        c = self.cache0
+        self._lib.call("mb_attention_decode_bf16", self.q.data_ptr(), self.hq * 128,
+                       c.k.data_ptr(), c.v.data_ptr(), c.block_table.data_ptr(), c.max_pages,
+                       self.kvl.data_ptr(), self.L + 1, self.B, self.hq, self.hkv, 128,
+                       self.ao.data_ptr(), self.hq * 128, self.aws.data_ptr(), self.aws_bytes,
+                       self._ops._stream())
+
+    dominant = "attn_decode_mma_kernel (one layer's KV read)"
+
+    def work_per_step(self):
+        return float(self.B)  # tokens
+
+    def roofline_work(self):
+        return 2.0 * self.B * (self.L + 1) * self.hkv * 128 * 2  # K and V bytes read
+
+    def e2e_step(self):
+        self.x.copy_(self.h_x, non_blocking=True)
+        y = self.stack.replay()
+        self.h_y.copy_(y, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.B * self.D * 2, self.B * self.D * 2
+
+    def cpu_sample(self, threads):
+        """One layer of the stack on the CPU oracle for 8 of the 64 sequences
+        (KV 8192), extrapolated to 8 layers: tok/s = 8 / (8 * t_layer)."""
+        import numpy as np
+        import oracle.ops as O
+        rng = np.random.default_rng(4)
+        D, H, HKV, FF, Bs = self.D, self.H, self.HKV, self.FF, 8
+        W = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)
+             for s in [(D, D + 2 * HKV * 128), (D, D), (D, 2 * FF), (FF, D)]]
+        kp = rng.standard_normal((Bs, HKV, self.L, 128), dtype=np.float32)
+        vp = rng.standard_normal((Bs, HKV, self.L, 128), dtype=np.float32)
+        x = rng.standard_normal((Bs, 1, D), dtype=np.float32)
+        kw = dict(H=H, H_kv=HKV, base=500000.0, causal=True, k_past=kp, v_past=vp)
+        O.decoder_layer(x, *W, **kw)  # warm
+        t0, n = time.perf_counter(), 0
+        while n < 1 or time.perf_counter() - t0 < 10.0:
+            O.decoder_layer(x, *W, **kw)
+            n += 1
+        t_layer = (time.perf_counter() - t0) / n
+        return Bs / (self.LAYERS * t_layer), (
+            f"numpy oracle, 1 of 8 layers x {n} runs for {Bs} of 64 sequences at KV 8192 "
+            f"(fp32, {threads} BLAS threads), extrapolated x8 layers")
+
+
+WORKLOADS = {"transpose": TransposeF32, "decoder_stack": DecoderStackDecode}
+DEFAULT_WORKLOAD = "decoder_stack"
+
+
+def count_our_launches(torch, fn) -> dict:
+    """Kernels one step launches, from a CUDA-activity trace: ours (libmb200),
+    NCCL's and torch's (index arithmetic around our calls)."""
+    fn()
+    torch.cuda.synchronize()
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as p:
+        fn()
+        torch.cuda.synchronize()
+    out = {"ours": 0, "nccl": 0, "torch": 0}
+    for e in p.events():
+        if getattr(e, "device_type", None) is None or "cuda" not in str(e.device_type).lower():
+            continue
+        n = e.name
+        if n.startswith("Memcpy") or n.startswith("Memset"):
+            continue
+        if "nccl" in n.lower():
+            out["nccl"] += 1
+        elif n.startswith("void at::") or n.startswith("at::") or "at::native" in n:
+            out["torch"] += 1
+        else:
+            out["ours"] += 1
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -229,8 +365,8 @@ def run_reference(args, wl):
     value = statistics.median(vals)
     line = {"metric": wl.metric, "value": value, "unit": wl.unit, "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
-            "data": "synthetic", "config": wl.config,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
+            "dtype": wl.dtype, "data": "synthetic", "config": wl.config,
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
@@ -264,7 +400,8 @@ def main(argv=None):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     from metalbench_b200 import ops
     ops.init(local)
-    wl.setup(torch, rank, world)
+    wl.setup(torch, rank, world, local)
+    n_launch = count_our_launches(torch, wl.step)
 
     def barrier():
         if world > 1:
@@ -300,7 +437,7 @@ def main(argv=None):
     if sampler:
         sampler.stop()
     ms_step = ms_total / args.steps
-    value = wl.work_per_step() * world / (ms_total / 1e3 / args.steps)
+    value = wl.job_units(world) / (ms_total / 1e3 / args.steps)
 
     # ---- dominant kernel: per-launch CUDA-event duration --------------------
     nl = min(200, max(20, args.steps))
@@ -335,7 +472,7 @@ def main(argv=None):
     x1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(x0.elapsed_time(x1)) / ne
-    e2e_value = wl.work_per_step() * world / (e2e_ms / 1e3)
+    e2e_value = wl.job_units(world) / (e2e_ms / 1e3)
     h2d, d2h = wl.e2e_bytes()
 
     if rank != 0:
@@ -350,16 +487,18 @@ def main(argv=None):
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic", "config": wl.config,
         "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": r_unit,
                      "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)"
                      if peak_kind == "measured" else "fallback",
-                     "traffic": profile_traffic(wl.name), "launch_ms": launch_ms},
+                     "traffic": profile_traffic(wl.name), "launch_ms": launch_ms,
+                     "kernel": getattr(wl, "dominant", wl.name)},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": wl.kernels_per_step() * args.steps,
+        "gpu_launches": n_launch["ours"] * args.steps,
+        "gpu_launches_detail": {"per_step": n_launch, "timed_steps": args.steps},
         "clocks": sampler.summary() if sampler else None,
     }
     print(json.dumps(line), flush=True)

@@ -141,3 +141,26 @@ def test_prefill_baseline_shape_prefix_rows():
     ref = O.decoder_layer(x[:, :P], *W, H=H, H_kv=Hkv, base=base, causal=True)
     _check(got[:, :P], ref)
     assert np.isfinite(got).all()
+
+
+def test_stack_prefill_and_graph_decode_match_oracle():
+    """3-layer stack: causal prefill of 40 tokens, then one decode step replayed
+    from a CUDA graph; both equal oracle.decoder_stack over 41 tokens."""
+    import torch
+    from metalbench_b200.decoder import DecoderConfig
+    from metalbench_b200.stack import DecoderStack
+    rng = np.random.default_rng(8)
+    B, S, D, H, Hkv, FF, base, n = 2, 40, 512, 4, 2, 256, 500000.0, 3
+    Ws = [_weights(rng, D, H, Hkv, FF) for _ in range(n)]
+    x = O.round_bf16(rng.standard_normal((B, S + 1, D)).astype(np.float32))
+    cfg = DecoderConfig(D, H, Hkv, FF, rope_base=base)
+    st = DecoderStack(cfg, n, B, 128, weights=[[_bf(torch, w) for w in W] for W in Ws])
+    y0 = st.forward(_bf(torch, x[:, :S]), torch.zeros(B, dtype=torch.int32, device="cuda"))
+    xd = _bf(torch, x[:, S:])
+    sp = torch.full((B,), S, dtype=torch.int32, device="cuda")
+    st.capture_decode(xd, sp, S + 1)  # the capture warm-up re-writes the same slot
+    y1 = st.replay().clone()
+    got = np.concatenate([_np(torch, y0), _np(torch, y1)], axis=1)
+    ref = O.decoder_stack(x, Ws, H=H, H_kv=Hkv, base=base, causal=True)
+    _check(got, ref)
+    st.close()
