@@ -2,6 +2,7 @@
 // the device-pointer entry points. Binding numbers follow the reference
 // registry entries (mlx/kernels/common/registry.py, mlx/kernels/full/registry.py).
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -173,6 +174,105 @@ int prep_conv2d(const RunArgs& a, KernelState& st, cudaStream_t) {
   return MB_OK;
 }
 
+// llama_decoder_layer: registry full/registry.py:87-104 — x@0 [B*S, D],
+// W_qkv@1, W_o@2, W_gu@3, W_down@4 (bf16, reference (in, out) layout), y@5;
+// scalars S@6, D@7, H@8, H_kv@9, FF@10, base@11 (f32), eps@12 (f32).
+// Extensions (config): "batch" (B, default 1), "causal" (default 0, as the
+// reference hook), "past_len" (cached tokens before x, default 0) with the
+// already-rotated cache as optional inputs k_past@13, v_past@14
+// [B, H_kv, past_len, 128] bf16. Weight packing and cache set-up happen in
+// prepare (untimed); each timed launch is one mb_decoder_layer_forward.
+int prep_llama(const RunArgs& a, KernelState& st, cudaStream_t stream) {
+  const RunArgs::Buf *x, *wq, *wo, *wg, *wd, *y;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &wq));
+  TRY(need_buf(a, 2, MB_ROLE_INPUT, &wo));
+  TRY(need_buf(a, 3, MB_ROLE_INPUT, &wg));
+  TRY(need_buf(a, 4, MB_ROLE_INPUT, &wd));
+  TRY(need_buf(a, 5, MB_ROLE_OUTPUT, &y));
+  int64_t S, D, H, Hkv, FF;
+  TRY(need_scalar(a, 6, &S));
+  TRY(need_scalar(a, 7, &D));
+  TRY(need_scalar(a, 8, &H));
+  TRY(need_scalar(a, 9, &Hkv));
+  TRY(need_scalar(a, 10, &FF));
+  double base = 10000.0, eps = 1e-5;
+  a.scalar(11, &base);
+  a.scalar(12, &eps);
+  const int B = (int)a.config.num("batch", 1);
+  const int causal = (int)a.config.num("causal", 0);
+  const int past = (int)a.config.num("past_len", 0);
+  MB_REQUIRE(B >= 1 && S >= 1 && past >= 0, "llama_decoder_layer: bad batch/S/past_len");
+  for (const RunArgs::Buf* b : {x, wq, wo, wg, wd, y})
+    MB_REQUIRE(b->dtype == MB_BF16, "llama_decoder_layer: buffers must be bf16");
+  const int Dh = (int)(D / H);
+  MB_REQUIRE(x->bytes == (size_t)(B * S * D * 2) && y->bytes == x->bytes,
+             "llama_decoder_layer: x/y must be [batch*S, D] bf16");
+  MB_REQUIRE(wq->bytes == (size_t)(D * (D + 2 * Hkv * Dh) * 2) && wo->bytes == (size_t)(D * D * 2) &&
+                 wg->bytes == (size_t)(D * 2 * FF * 2) && wd->bytes == (size_t)(FF * D * 2),
+             "llama_decoder_layer: weight sizes do not match D/H/H_kv/FF");
+  mb_decoder_config cfg{(int)D, (int)H, (int)Hkv, Dh, (int)FF, (float)base, (float)eps};
+  void* layer = nullptr;
+  int rc = mb_decoder_layer_create(&cfg, (const uint16_t*)wq->dev, (const uint16_t*)wo->dev,
+                                   (const uint16_t*)wg->dev, (const uint16_t*)wd->dev, 0, 1, &layer);
+  if (rc) return rc;
+  st.cleanup.push_back([layer] { mb_decoder_layer_destroy(layer); });
+  const int kv_total = past + (int)S;
+  const int pages = (kv_total + 63) / 64;
+  const size_t page_elems = (size_t)Hkv * 64 * Dh;
+  auto alloc = [&](size_t bytes, void** p) -> int {
+    MB_CUDA(cudaMalloc(p, bytes));
+    st.scratch.push_back(*p);
+    return MB_OK;
+  };
+  void *kc, *vc, *bt, *spos, *kvl;
+  TRY(alloc((size_t)B * pages * page_elems * 2, &kc));
+  TRY(alloc((size_t)B * pages * page_elems * 2, &vc));
+  TRY(alloc((size_t)B * pages * 4, &bt));
+  TRY(alloc((size_t)B * 4, &spos));
+  TRY(alloc((size_t)B * 4, &kvl));
+  std::vector<int> h_bt(B * pages), h_sp(B, past), h_kl(B, kv_total);
+  for (int i = 0; i < B * pages; ++i) h_bt[i] = i;
+  MB_CUDA(cudaMemcpy(bt, h_bt.data(), h_bt.size() * 4, cudaMemcpyHostToDevice));
+  MB_CUDA(cudaMemcpy(spos, h_sp.data(), h_sp.size() * 4, cudaMemcpyHostToDevice));
+  MB_CUDA(cudaMemcpy(kvl, h_kl.data(), h_kl.size() * 4, cudaMemcpyHostToDevice));
+  MB_CUDA(cudaMemset(kc, 0, (size_t)B * pages * page_elems * 2));
+  MB_CUDA(cudaMemset(vc, 0, (size_t)B * pages * page_elems * 2));
+  if (past > 0) {
+    const RunArgs::Buf *kp = a.buf(13), *vp = a.buf(14);
+    MB_REQUIRE(kp && vp && kp->bytes == (size_t)B * Hkv * past * Dh * 2 && vp->bytes == kp->bytes,
+               "llama_decoder_layer: past_len > 0 needs k_past@13 and v_past@14 [B, H_kv, past_len, Dh]");
+    // [B][Hkv][past][Dh] -> pages [b*pages + p][Hkv][64][Dh], one 2-D copy per (b, page)
+    for (int b = 0; b < B; ++b)
+      for (int p = 0; p * 64 < past; ++p) {
+        const int rows = past - p * 64 < 64 ? past - p * 64 : 64;
+        const size_t src_off = (((size_t)b * Hkv) * past + (size_t)p * 64) * Dh * 2;
+        const size_t dst_off = ((size_t)b * pages + p) * page_elems * 2;
+        for (int which = 0; which < 2; ++which) {
+          const uint8_t* src = (const uint8_t*)(which ? vp->dev : kp->dev) + src_off;
+          uint8_t* dst = (uint8_t*)(which ? vc : kc) + dst_off;
+          MB_CUDA(cudaMemcpy2DAsync(dst, (size_t)64 * Dh * 2, src, (size_t)past * Dh * 2,
+                                    (size_t)rows * Dh * 2, (size_t)Hkv, cudaMemcpyDeviceToDevice,
+                                    stream));
+        }
+      }
+  }
+  const size_t wsb = mb_decoder_layer_workspace_bytes(layer, B, (int)S, kv_total);
+  void* ws = nullptr;
+  TRY(alloc(wsb, &ws));
+  MB_CUDA(cudaStreamSynchronize(stream));
+  const void* px = x->dev;
+  void* py = y->dev;
+  st.threads_per_cta = 256;
+  st.launches_per_iter = 0;  // several kernels; see the profiles
+  st.launch = [=](cudaStream_t s) {
+    return mb_decoder_layer_forward(layer, (const uint16_t*)px, (uint16_t*)py, B, (int)S,
+                                    (const int*)spos, (const int*)kvl, kv_total, (uint16_t*)kc,
+                                    (uint16_t*)vc, (const int*)bt, pages, causal, ws, wsb, s);
+  };
+  return MB_OK;
+}
+
 }  // namespace
 
 void register_all_kernels() {
@@ -183,6 +283,7 @@ void register_all_kernels() {
     register_kernel({"sqr_mm", prep_sqr_mm});
     register_kernel({"gemm_bf16", prep_gemm_bf16});
     register_kernel({"conv2d", prep_conv2d});
+    register_kernel({"llama_decoder_layer", prep_llama});
   });
 }
 

@@ -1,4 +1,4 @@
-"""``mlx.core`` subset on numpy (test infrastructure; see package docstring)."""
+"""``mlx.core`` subset on numpy (see package docstring)."""
 from __future__ import annotations
 
 import numpy as np
@@ -27,8 +27,9 @@ def matmul(a, b):
 
 
 def transpose(a, axes=None):
-    """MLX default reverses all axes, like numpy."""
-    return np.transpose(a, axes)
+    """MLX default reverses all axes, like numpy. The result is materialised
+    (a contiguous copy) so a timed reference call does the data movement."""
+    return np.ascontiguousarray(np.transpose(a, axes))
 
 
 def mean(a, axis=None, keepdims=False):
@@ -112,3 +113,20 @@ class _Random:
 
 
 random = _Random()
+
+
+def swapaxes(a, axis1, axis2):
+    """Materialised like ``transpose``."""
+    return np.ascontiguousarray(np.swapaxes(a, axis1, axis2))
+
+
+def where(cond, x, y):
+    return np.where(cond, x, y)
+
+
+def maximum(a, b):
+    return np.maximum(a, b)
+
+
+def astype(a, dtype):
+    return np.asarray(a).astype(dtype)

@@ -1,4 +1,4 @@
-"""``mlx.nn`` subset on numpy (test infrastructure; see package docstring)."""
+"""``mlx.nn`` subset on numpy (see package docstring)."""
 import numpy as np
 
 

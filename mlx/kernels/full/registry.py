@@ -1,0 +1,54 @@
+"""Full-set registry entries served by the B200 backend (format: see
+mlx/kernels/common/registry.py). The reference's own entry
+(mlx/kernels/full/registry.py:87-104: S=64, D=128, H=4, H_kv=2, head_dim 32)
+is replaced by the BASELINE.json decoder configurations: libmb200's decoder
+kernels need head_dim 128 and d_model a multiple of 256.
+"""
+D, H, HKV, FF, DH = 4096, 32, 8, 14336, 128
+NQKV = D + 2 * HKV * DH
+_W = [(D, NQKV), (D, D), (D, 2 * FF), (FF, D)]
+_PARAMS = D * NQKV + D * D + D * 2 * FF + FF * D
+_SCALARS = [dict(binding=6, dtype="u32", value=0), dict(binding=7, dtype="u32", value=D),
+            dict(binding=8, dtype="u32", value=H), dict(binding=9, dtype="u32", value=HKV),
+            dict(binding=10, dtype="u32", value=FF), dict(binding=11, dtype="f32", value=500000.0),
+            dict(binding=12, dtype="f32", value=1e-5)]
+
+
+def _scalars(S):
+    out = [dict(s) for s in _SCALARS]
+    out[0]["value"] = S
+    return out
+
+
+REGISTRY = {}
+
+# prefill: batch 4 x seq 2048, causal
+_B, _S = 4, 2048
+REGISTRY["llama_decoder_layer"] = dict(
+    kernel="llama_decoder_layer", metal_function="llama_decoder_layer_f32",
+    input_bindings=(0, 1, 2, 3, 4),
+    input_shapes=[(_B, _S, D)] + _W, input_dtypes=["bf16"] * 5,
+    input_init=[("normal", 1.0)] + [("normal", 0.02)] * 4,
+    output_shape=(_B, _S, D), output_dtype="bf16",
+    scalars=_scalars(_S), config={"batch": _B, "causal": 1},
+    model_kwargs=dict(S=_S, D=D, H=H, H_kv=HKV, FF=FF, base=500000.0, eps=1e-5, causal=True),
+    rtol=2e-2, atol=2e-2, seed=3,
+    flops=2 * _PARAMS * _B * _S + 2 * 2 * _B * H * DH * (_S * (_S + 1) // 2),
+    bytes=2 * (_PARAMS + 2 * _B * _S * D),
+    roof="tensor_bf16", ref_warmup=0, ref_iters=1)
+
+# decode: batch 32, one new token after a 4096-token cache
+_BD, _L = 32, 4096
+REGISTRY["llama_decoder_layer_decode"] = dict(
+    kernel="llama_decoder_layer", metal_function="llama_decoder_layer_f32",
+    input_bindings=(0, 1, 2, 3, 4, 13, 14),
+    input_shapes=[(_BD, 1, D)] + _W + [(_BD, HKV, _L, DH)] * 2, input_dtypes=["bf16"] * 7,
+    input_init=[("normal", 1.0)] + [("normal", 0.02)] * 4 + [("normal", 1.0)] * 2,
+    output_shape=(_BD, 1, D), output_dtype="bf16",
+    scalars=_scalars(1), config={"batch": _BD, "causal": 1, "past_len": _L},
+    model_kwargs=dict(S=1, D=D, H=H, H_kv=HKV, FF=FF, base=500000.0, eps=1e-5, causal=True),
+    hook="llama_decoder_layer",
+    rtol=2e-2, atol=2e-2, seed=3,
+    flops=2 * _PARAMS * _BD + 2 * 2 * _BD * H * DH * (_L + 1),
+    bytes=2 * _PARAMS + 2 * 2 * _BD * HKV * _L * DH,
+    roof="hbm", ref_warmup=0, ref_iters=2)

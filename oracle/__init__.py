@@ -12,13 +12,13 @@ hooks on the hot path:
 * ``mlx/kernels/common/conv2d.py:7-12``         NHWC x OHWI cross-correlation
 * ``mlx/kernels/full/llama_decoder_layer.py:24-64`` the LLaMA decoder layer
 
-``oracle.mlx_shim`` is a numpy implementation of the small ``mlx.core`` /
-``mlx.nn`` subset those hook files use. ``tests/golden/gen_golden.py`` uses it to
-execute the reference's own hook files (not our restatement) and commits their
-outputs as fixtures; the restatement is pinned against those fixtures.
+``tests/golden/gen_golden.py`` executes the reference's own hook files (not
+this restatement) through ``metalbench_b200/mlx_compat`` (a numpy stand-in for
+the MLX ops they use) and commits their outputs as fixtures; the restatement
+is pinned against those fixtures (tests/test_oracle.py).
 
 Parity status: pinned against the reference hook code executed through the
-numpy shim. MLX itself (a third-party dependency, ``mlx>=0.18.0`` in the
+numpy MLX stand-in. MLX itself (a third-party dependency, ``mlx>=0.18.0`` in the
 reference's requirements.txt:1) is absent here, so the shim's op semantics are
 restated from MLX's published API, not run.
 """

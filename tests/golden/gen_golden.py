@@ -4,8 +4,8 @@ Run in the build container (where the read-only reference checkout exists):
 
     python tests/golden/gen_golden.py [--reference PATH]
 
-MLX is not installed here, so ``oracle/mlx_shim`` (a numpy implementation of
-the MLX ops the hooks use) is put on ``sys.path`` as ``mlx``. The script then
+MLX is not installed here, so ``metalbench_b200/mlx_compat`` (a numpy
+implementation of the MLX ops the hooks use) is put on ``sys.path`` as ``mlx``. The script then
 loads each hook (``mlx/kernels/<set>/<name>.py``) from the reference checkout,
 builds its ``Model`` exactly as the reference harness does
 (mlx/scripts/mlx_helpers.py:219-257: ``Model()`` with default arguments and one
@@ -55,8 +55,8 @@ def main(argv=None):
         import mlx.core  # noqa: F401
         print("[golden] using real mlx", file=sys.stderr)
     except ImportError:
-        sys.path.insert(0, str(REPO / "oracle" / "mlx_shim"))
-        print("[golden] mlx absent: using oracle/mlx_shim", file=sys.stderr)
+        sys.path.insert(0, str(REPO / "metalbench_b200" / "mlx_compat"))
+        print("[golden] mlx absent: using metalbench_b200/mlx_compat", file=sys.stderr)
     import mlx.core as mx
 
     for name, kset, shapes, seed in CASES:
