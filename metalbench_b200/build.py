@@ -100,6 +100,13 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         p = subprocess.run(link, capture_output=True, text=True)
         if p.returncode != 0:
             raise RuntimeError(f"link failed:\n{p.stdout}\n{p.stderr}")
+    host_src = PKG / "host" / "mb200_host.cpp"
+    if force or _stale(HOST, [host_src, LIB] + headers):
+        cmd = ["g++", "-O2", "-std=c++17", "-I", str(REPO / "include"), str(host_src), "-o",
+               str(HOST), "-L", str(PKG), "-l:libmb200.so", "-Wl,-rpath,$ORIGIN"]
+        p = subprocess.run(cmd, capture_output=True, text=True)
+        if p.returncode != 0:
+            raise RuntimeError(f"mb200_host build failed:\n{p.stdout}\n{p.stderr}")
     return LIB
 
 
