@@ -16,6 +16,8 @@
 // image, which is exactly the zero padding, and lands the box as 128 rows of
 // 128 bytes in the same 128-byte swizzle as a K-major GEMM operand. The weight
 // tensor [Cout, KH*KW*Cin] is the K-major B operand as stored (OHWI).
+#include <stdlib.h>
+
 #include "gemm_core.cuh"
 #include "gemm_epi.cuh"
 
@@ -33,6 +35,9 @@ struct ConvProducer {
   ConvGeom g;
   static constexpr int KE = 64;
   static constexpr uint32_t BYTES = (BM + BN) * KBYTES;
+  static constexpr int STAGE_BYTES = (BM + BN) * KBYTES;
+  static constexpr int RESIDENT_BYTES = 0;
+  __device__ uint32_t resident_tx_bytes() const { return 0; }
   static constexpr int KSTEPS = 4;
   __device__ void prefetch() const {
     mbd::prefetch_tmap(&x);
@@ -52,6 +57,64 @@ struct ConvProducer {
   }
   __device__ static uint64_t b_desc(uint32_t sB, int kk) {
     return mbd::sw128_desc(sB + kk * 32, 16, 1024);
+  }
+  __device__ void load_resident(uint8_t*, uint64_t*) const {}
+  __device__ void issue(uint32_t d, uint32_t st, uint32_t, int, bool first) const {
+    constexpr uint32_t idesc = mbd::make_idesc(1u, BM, BN, 0, 0);
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk)
+      mbd::mma_f16(d, a_desc(st, kk), b_desc(st + BM * KBYTES, kk), idesc,
+                   (!first || kk > 0) ? 1u : 0u);
+  }
+};
+
+// Resident-weight variant (weights of all taps fit in shared memory next to
+// the ring): the whole [Cout, KH*KW*Cin] weight is loaded once per CTA, and a
+// stage is ONE TMA box {64 ch, TW, TH+KH-1, 1} taken at filter column s and
+// channel chunk c0. The KH filter rows r are then just descriptor offsets of
+// r*TW rows (r*TW*128 bytes, a multiple of the 1024-byte swizzle atom) into
+// that box, so one load serves KH taps: A traffic per tile drops from
+// KH*KW boxes of 128 rows to KW boxes of (TH+KH-1)*TW rows, and B is never
+// reloaded. k-block kb = (s, channel chunk).
+template <int BN, int KH>
+struct ConvResProducer {
+  CUtensorMap x, w;
+  ConvGeom g;
+  int box_rows;  // TH + KH - 1
+  static constexpr int STAGE_BYTES = 4 * 64 * KBYTES;  // max (TH+KH-1)*TW*128 served: 32 KiB
+  static constexpr int MAX_TAPS_CHUNKS = 9;             // KH*KW*cchunks served resident
+  static constexpr int RESIDENT_BYTES = MAX_TAPS_CHUNKS * BN * KBYTES;
+  static constexpr uint32_t BYTES = STAGE_BYTES;
+  uint32_t resident_tx;  // bytes of the resident weight load
+  __device__ uint32_t resident_tx_bytes() const { return resident_tx; }
+  __device__ void prefetch() const {
+    mbd::prefetch_tmap(&x);
+    mbd::prefetch_tmap(&w);
+  }
+  __device__ void load_resident(uint8_t* res, uint64_t* bar) const {
+    const int chunks = g.KH * g.KW * g.cchunks;
+    for (int j = 0; j < chunks; ++j) mbd::tma_load_2d(res + j * BN * KBYTES, &w, bar, j * 64, 0);
+  }
+  __device__ void load(uint8_t* st, uint64_t* bar, int tm, int, int kb) const {
+    const int tw = tm % g.tiles_w;
+    const int th = (tm / g.tiles_w) % g.tiles_h;
+    const int n = tm / (g.tiles_w * g.tiles_h);
+    const int s = kb / g.cchunks, c0 = (kb % g.cchunks) * 64;
+    mbd::tma_load_4d(st, &x, bar, c0, tw * g.TW + s - g.pad, th * g.TH - g.pad, n);
+  }
+  __device__ void issue(uint32_t d, uint32_t st, uint32_t res, int kb, bool first) const {
+    constexpr uint32_t idesc = mbd::make_idesc(1u, BM, BN, 0, 0);
+    const int s = kb / g.cchunks, cc = kb % g.cchunks;
+#pragma unroll
+    for (int r = 0; r < KH; ++r) {
+      const int j = (r * g.KW + s) * g.cchunks + cc;  // weight chunk of tap (r, s), chunk cc
+      const uint32_t a = st + r * g.TW * KBYTES, b = res + j * BN * KBYTES;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mbd::mma_f16(d, mbd::sw128_desc(a + kk * 32, 16, 1024),
+                     mbd::sw128_desc(b + kk * 32, 16, 1024), idesc,
+                     (!first || r > 0 || kk > 0) ? 1u : 0u);
+    }
   }
 };
 
@@ -84,8 +147,8 @@ struct EpiConv {
 template <int BN, int STAGES>
 int launch_conv(const uint16_t* x, const uint16_t* w, uint16_t* y, const ConvGeom& g,
                 cudaStream_t stream) {
-  using S = Smem<Mode::BF16, BN, STAGES>;
   using P = ConvProducer<BN>;
+  using S = Smem<P, BN, STAGES>;
   using E = EpiConv<BN>;
   P p;
   p.g = g;
@@ -110,7 +173,52 @@ int launch_conv(const uint16_t* x, const uint16_t* w, uint16_t* y, const ConvGeo
   e.M = sc.tiles_m * BM;
   e.g = g;
   e.y = y;
-  auto kern = gemm_kernel<Mode::BF16, BN, STAGES, false, P, E>;
+  auto kern = gemm_kernel<BN, STAGES, P, E>;
+  static bool attr = false;
+  if (!attr) {
+    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr = true;
+  }
+  const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
+  kern<<<grid, 256, S::TOTAL, stream>>>(p, e, sc, mb::device_status_ptr());
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+template <int BN, int KH, int STAGES>
+int launch_conv_res(const uint16_t* x, const uint16_t* w, uint16_t* y, const ConvGeom& g,
+                    cudaStream_t stream) {
+  using P = ConvResProducer<BN, KH>;
+  using S = Smem<P, BN, STAGES>;
+  using E = EpiConv<BN>;
+  static_assert(S::TOTAL <= 232448, "conv: shared memory over the sm_100 limit");
+  P p;
+  p.g = g;
+  p.box_rows = g.TH + KH - 1;
+  const int chunks = g.KH * g.KW * g.cchunks;
+  p.resident_tx = (uint32_t)(chunks * BN * KBYTES);
+  const uint64_t dims[4] = {(uint64_t)g.C, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.N};
+  const uint64_t strides[3] = {(uint64_t)g.C * 2, (uint64_t)g.W * g.C * 2,
+                               (uint64_t)g.H * g.W * g.C * 2};
+  const uint32_t box[4] = {64, (uint32_t)g.TW, (uint32_t)p.box_rows, 1};
+  int rc = mb::make_tmap_nd(&p.x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const int64_t Kt = (int64_t)g.KH * g.KW * g.C;
+  rc = mb::make_tmap_2d(&p.w, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Kt, g.Co, Kt * 2, 64, BN,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  Sched sc;
+  sc.tiles_m = g.N * g.tiles_h * g.tiles_w;
+  sc.tiles_n = 1;
+  sc.kblocks = g.KW * g.cchunks;
+  sc.ksplit = 1;
+  sc.kb_per_split = sc.kblocks;
+  E e;
+  e.M = sc.tiles_m * BM;
+  e.g = g;
+  e.y = y;
+  auto kern = gemm_kernel<BN, STAGES, P, E>;
   static bool attr = false;
   if (!attr) {
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
@@ -146,6 +254,11 @@ extern "C" int mb_conv2d_nhwc_bf16(const uint16_t* x, const uint16_t* w, uint16_
   g.tiles_h = (g.H2 + g.TH - 1) / g.TH;
   g.cchunks = Cin / 64;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Resident-weight path: 64-wide output tiles, 3 filter rows, all weight
+  // chunks (KH*KW*Cin/64 <= 9) in shared memory, Cout <= 64.
+  if (g.TW == 64 && KH == 3 && KH * KW * g.cchunks <= 9 && Cout <= 64 &&
+      getenv("MB_CONV_NO_RESIDENT") == nullptr)
+    return launch_conv_res<64, 3, 4>(x, w, y, g, s);
   if (Cout <= 64) return launch_conv<64, 8>(x, w, y, g, s);
   if (Cout <= 128) return launch_conv<128, 6>(x, w, y, g, s);
   return launch_conv<256, 4>(x, w, y, g, s);

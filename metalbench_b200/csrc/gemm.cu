@@ -115,7 +115,7 @@ extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M
   MB_CUDA(cudaGetLastError());
 
   using P = GemmProducer<Mode::TF32X3, 128, false>;
-  using S = Smem<Mode::TF32X3, 128, 3>;
+  using S = Smem<P, 128, 3>;
   gemm::Epi<128, gemm::EpiStore> e{};
   e.M = (int)M;
   e.N = (int)N;
@@ -137,7 +137,7 @@ extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M
   sc.kblocks = (int)((K + P::KE - 1) / P::KE);
   sc.ksplit = 1;
   sc.kb_per_split = sc.kblocks;
-  auto kern = gemm_kernel<Mode::TF32X3, 128, 3, false, P, decltype(e)>;
+  auto kern = gemm_kernel<128, 3, P, decltype(e)>;
   static bool attr = false;
   if (!attr) {
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
@@ -233,7 +233,7 @@ extern "C" int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, i
   MB_CUDA(cudaGetLastError());
 
   using P = GemmProducer<Mode::TF32X3, 128, false>;
-  using S = Smem<Mode::TF32X3, 128, 3>;
+  using S = Smem<P, 128, 3>;
   gemm::Epi<128, gemm::EpiStore> e{};
   e.M = (int)M;
   e.N = (int)N;
@@ -255,7 +255,7 @@ extern "C" int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, i
   sc.kblocks = (int)((K + P::KE - 1) / P::KE);
   sc.ksplit = 1;
   sc.kb_per_split = sc.kblocks;
-  auto kern = gemm_kernel<Mode::TF32X3, 128, 3, false, P, decltype(e)>;
+  auto kern = gemm_kernel<128, 3, P, decltype(e)>;
   MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
   const int grid = sc.total() < sms ? sc.total() : sms;
   kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, slot->status);

@@ -31,18 +31,17 @@ constexpr int KBYTES = 128;  // K extent of one stage in bytes (one swizzle row)
 enum class Mode { BF16 = 0, TF32X3 = 1 };
 
 __host__ __device__ constexpr int elem_bytes(Mode m) { return m == Mode::BF16 ? 2 : 4; }
-__host__ __device__ constexpr int num_warps(Mode) { return 8; }
 
-template <Mode MODE, int BN, int STAGES>
+// Shared-memory plan: [resident operand (optional)][STAGES x stage][barriers].
+template <class Producer, int BN, int STAGES>
 struct Smem {
-  static constexpr int A_BYTES = BM * KBYTES;
-  static constexpr int B_BYTES = BN * KBYTES;
-  static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;  // hi (+ lo)
-  static constexpr int STAGE_BYTES = PARTS * (A_BYTES + B_BYTES);
+  static constexpr int RES_BYTES = (Producer::RESIDENT_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGE_BYTES = Producer::STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  // barriers: full, empty per stage; tfull, tempty x2; tmem slot, abort, drain
-  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
-  static constexpr int TOTAL = 1024 /*alignment slack*/ + RING_BYTES + BAR_BYTES;
+  // barriers: full, empty per stage; tfull, tempty x2; resident;
+  // then tmem slot, abort flag, drain barrier
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int TOTAL = 1024 /*alignment slack*/ + RES_BYTES + RING_BYTES + BAR_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
 };
 
@@ -94,6 +93,9 @@ struct GemmProducer {
   static constexpr int KE = KBYTES / elem_bytes(MODE);  // K elements per stage
   static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;
   static constexpr uint32_t BYTES = PARTS * (BM + BN) * KBYTES;
+  static constexpr int STAGE_BYTES = PARTS * (BM + BN) * KBYTES;
+  static constexpr int RESIDENT_BYTES = 0;
+  __device__ uint32_t resident_tx_bytes() const { return 0; }
   static constexpr int B_BOX_BYTES = KE * KBYTES;       // one MN-major box
   static_assert(MODE == Mode::BF16 || !B_MN, "TF32x3 operands are K-major");
   __device__ void prefetch() const {
@@ -132,30 +134,50 @@ struct GemmProducer {
     constexpr int step = MODE == Mode::BF16 ? 2048 : 1024;
     return mbd::sw128_desc(sB + kk * step, B_BOX_BYTES, 1024);
   }
+  __device__ void load_resident(uint8_t*, uint64_t*) const {}
+  // All MMAs of one stage into accumulator d; `first` starts a fresh sum.
+  __device__ void issue(uint32_t d, uint32_t st, uint32_t /*res*/, int /*kb*/, bool first) const {
+    constexpr uint32_t fmt = MODE == Mode::BF16 ? 1u : 2u;
+    constexpr uint32_t idesc = mbd::make_idesc(fmt, BM, BN, 0, B_MN ? 1u : 0u);
+    const uint32_t a0 = st, b0 = st + BM * KBYTES;
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+      const uint64_t ad = a_desc(a0, kk), bd = b_desc(b0, kk);
+      if constexpr (MODE == Mode::BF16) {
+        mbd::mma_f16(d, ad, bd, idesc, acc);
+      } else {
+        // stage layout [A hi][B hi][A lo][B lo]
+        const uint32_t alo = b0 + BN * KBYTES, blo = alo + BM * KBYTES;
+        mbd::mma_tf32(d, a_desc(alo, kk), bd, idesc, acc);  // lo * hi
+        mbd::mma_tf32(d, ad, b_desc(blo, kk), idesc, 1u);   // hi * lo
+        mbd::mma_tf32(d, ad, bd, idesc, 1u);                // hi * hi
+      }
+    }
+  }
 };
 
-template <Mode MODE, int BN, int STAGES, bool B_MN, class Producer, class Epi>
-__global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
+template <int BN, int STAGES, class Producer, class Epi>
+__global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ Producer prod, const __grid_constant__ Epi epi,
                 const Sched sched, uint32_t* status) {
-  using S = Smem<MODE, BN, STAGES>;
+  using S = Smem<Producer, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(base + S::RING_BYTES);
+  uint8_t* res = base;  // resident operand (Producer::RESIDENT_BYTES)
+  uint8_t* ring = base + S::RES_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + S::RING_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* res_full = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* drain = reinterpret_cast<uint64_t*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto sA = [&](int s) { return base + s * S::STAGE_BYTES; };
-  auto sB = [&](int s) { return base + s * S::STAGE_BYTES + S::A_BYTES; };
-  // TF32x3: the "lo" halves follow the hi halves of the stage.
-  auto sAlo = [&](int s) { return base + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
-  auto sBlo = [&](int s) { return base + s * S::STAGE_BYTES + 2 * S::A_BYTES + S::B_BYTES; };
+  auto sA = [&](int s) { return ring + s * S::STAGE_BYTES; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -167,6 +189,7 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
       mbd::mbar_init(&tempty[b], 128);
     }
     mbd::mbar_init(drain, 1);
+    mbd::mbar_init(res_full, 1);
     *abort_flag = 0;
     mbd::fence_mbar_init();
   }
@@ -185,6 +208,10 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
       uint32_t issued = 0;  // bit s: parity of the last load issued into stage s
       uint32_t used = 0;    // bit s: stage s received at least one load
       bool ok = true;
+      if constexpr (Producer::RESIDENT_BYTES > 0) {
+        mbd::mbar_expect_tx(res_full, prod.resident_tx_bytes());
+        prod.load_resident(res, res_full);
+      }
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         int tm, tn, ks, kb0, kb1;
         sched.get(t, tm, tn, ks);
@@ -208,15 +235,17 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
       // release: wait (bounded) for the last load of every stage.
       for (int s = 0; s < STAGES; ++s)
         if (used & (1u << s)) mbd::mbar_wait(&full[s], (issued >> s) & 1, status, MB_DEV_TIMEOUT_TMA);
+      if constexpr (Producer::RESIDENT_BYTES > 0) mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_TMA);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t fmt = MODE == Mode::BF16 ? 1u : 2u;
-      constexpr uint32_t idesc = mbd::make_idesc(fmt, BM, BN, 0, B_MN ? 1u : 0u);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      if constexpr (Producer::RESIDENT_BYTES > 0)
+        ok = mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_MMA, abort_flag);
+      const uint32_t res_u32 = mbd::smem_u32(res);
       int i = 0;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++i) {
         int tm, tn, ks, kb0, kb1;
@@ -233,21 +262,7 @@ __global__ void __launch_bounds__(num_warps(MODE) * 32, 1)
             break;
           }
           mbd::tc_fence_after();
-          const uint32_t a0 = mbd::smem_u32(sA(stage)), b0 = mbd::smem_u32(sB(stage));
-#pragma unroll
-          for (int kk = 0; kk < Producer::KSTEPS; ++kk) {
-            const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
-            const uint64_t ad = Producer::a_desc(a0, kk), bd = Producer::b_desc(b0, kk);
-            if constexpr (MODE == Mode::BF16) {
-              mbd::mma_f16(d, ad, bd, idesc, acc);
-            } else {
-              const uint64_t adl = Producer::a_desc(mbd::smem_u32(sAlo(stage)), kk);
-              const uint64_t bdl = Producer::b_desc(mbd::smem_u32(sBlo(stage)), kk);
-              mbd::mma_tf32(d, adl, bd, idesc, acc);  // lo * hi
-              mbd::mma_tf32(d, ad, bdl, idesc, 1u);   // hi * lo
-              mbd::mma_tf32(d, ad, bd, idesc, 1u);    // hi * hi
-            }
-          }
+          prod.issue(d, mbd::smem_u32(sA(stage)), res_u32, kb, kb == kb0);
           mbd::mma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;

@@ -7,8 +7,8 @@ namespace gemm {
 template <Mode MODE, int BN, int STAGES, bool B_MN, class Epi>
 inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, int64_t N, int64_t K,
                 int ksplit, cudaStream_t stream) {
-  using S = Smem<MODE, BN, STAGES>;
   using P = GemmProducer<MODE, BN, B_MN>;
+  using S = Smem<P, BN, STAGES>;
   const int esz = elem_bytes(MODE);
   const CUtensorMapDataType dt =
       MODE == Mode::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -35,14 +35,14 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
   sc.kb_per_split = (sc.kblocks + sc.ksplit - 1) / sc.ksplit;
   // no empty trailing split: every split owns at least one k-block
   sc.ksplit = (sc.kblocks + sc.kb_per_split - 1) / sc.kb_per_split;
-  auto kern = gemm_kernel<MODE, BN, STAGES, B_MN, P, Epi>;
+  auto kern = gemm_kernel<BN, STAGES, P, Epi>;
   static bool attr = false;  // one instantiation = one static
   if (!attr) {
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
     attr = true;
   }
   const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
-  kern<<<grid, num_warps(MODE) * 32, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
+  kern<<<grid, 256, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
