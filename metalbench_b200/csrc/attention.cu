@@ -439,13 +439,15 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
 }  // namespace
 
 namespace {
-// Pages per split: aim for about two CTAs per SM over all (sequence, kv head).
+// Pages per split: about 12 CTAs per SM over all (sequence, kv head) units,
+// so the last partial wave is short, but at least 4 pages (64 KiB of K+V) per
+// CTA so the ring has work to overlap.
 int decode_split_pages(int B, int Hkv, int max_kv_len, int* splits) {
   const int units = B * Hkv;
   const int pages = (max_kv_len + PAGE - 1) / PAGE;
-  const int want = (2 * mb::num_sms() + units - 1) / units;
+  const int want = (12 * mb::num_sms() + units - 1) / units;
   int pps = (pages + want - 1) / want;
-  if (pps < 1) pps = 1;
+  if (pps < 4) pps = 4;
   *splits = (pages + pps - 1) / pps;
   return pps;
 }
