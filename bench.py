@@ -316,7 +316,88 @@ class DecoderStackDecode(Workload):
             f"(fp32, {threads} BLAS threads), extrapolated x8 layers")
 
 
-WORKLOADS = {"transpose": TransposeF32, "decoder_stack": DecoderStackDecode}
+class ShardedGemm(Workload):
+    """bf16 GEMM C = A @ B at 16384^3 ("a sharded bf16 GEMM
+    16384x16384x16384"), A, B ~ N(0,1) seed 4, column-sharded over the GPUs:
+    rank r holds all of A and the column block B[:, r*N/P:(r+1)*N/P] and
+    computes its block of C (no collective on the hot path). Strong scaling:
+    the job is one 16384^3 product at every N."""
+    name = "gemm_bf16_16384"
+    metric = "sharded bf16 GEMM 16384^3 throughput"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    bound = "tensor"
+    scaling = "strong"
+    default_steps = 20
+    M = N = K = 16384
+
+    def __init__(self):
+        self.config = {"workload": "gemm_bf16_16384", "M": self.M, "N": self.N, "K": self.K,
+                       "layout": "A [M,K] row-major, B [K,N] row-major (column block per rank)",
+                       "l2": "inputs larger than L2 (512 MiB per operand)"}
+
+    def setup(self, torch, rank, world, local):
+        from metalbench_b200 import ops
+        self.ops, self.torch = ops, torch
+        self.config["parallelism"] = f"column-shard x{world}"
+        self.nloc = self.N // world
+        g = torch.Generator(device="cuda").manual_seed(4)
+        self.a = torch.randn((self.M, self.K), generator=g, device="cuda").bfloat16()
+        b = torch.randn((self.K, self.N), generator=g, device="cuda").bfloat16()
+        self.b = b[:, rank * self.nloc:(rank + 1) * self.nloc].contiguous()
+        del b
+        self.c = torch.empty((self.M, self.nloc), device="cuda", dtype=torch.bfloat16)
+        self.h_a = torch.empty_like(self.a, device="cpu").pin_memory()
+        self.h_a.copy_(self.a)
+        self.h_b = torch.empty_like(self.b, device="cpu").pin_memory()
+        self.h_b.copy_(self.b)
+        self.h_c = torch.empty_like(self.c, device="cpu").pin_memory()
+        torch.cuda.empty_cache()
+
+    def step(self):
+        self.ops.gemm_bf16(self.a, self.b, self.c, b_layout="kn")
+
+    launch_dominant = step
+    dominant = "gemm_kernel<256,4,GemmProducer<bf16,256,MN-major B>> (this rank's column block)"
+
+    def work_per_step(self):
+        return 2.0 * self.M * self.N * self.K / 1e12  # TFLOP per step (whole job)
+
+    def job_units(self, world):
+        return self.work_per_step()
+
+    def roofline_work(self):
+        return 2.0 * self.M * self.nloc * self.K  # FLOP per launch on this rank
+
+    def e2e_step(self):
+        self.a.copy_(self.h_a, non_blocking=True)
+        self.b.copy_(self.h_b, non_blocking=True)
+        self.step()
+        self.h_c.copy_(self.c, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.a.numel() * 2 + self.b.numel() * 2, self.c.numel() * 2
+
+    def cpu_sample(self, threads):
+        """numpy fp32 GEMM on 2048 rows of A (the full B), scaled to TFLOP/s."""
+        import numpy as np
+        import oracle.ops as O
+        rng = np.random.default_rng(4)
+        a = rng.standard_normal((2048, self.K), dtype=np.float32)
+        b = rng.standard_normal((self.K, 2048), dtype=np.float32)
+        O.sqr_mm(a, b, acc=np.float32)
+        t0, n = time.perf_counter(), 0
+        while n < 1 or time.perf_counter() - t0 < 10.0:
+            O.sqr_mm(a, b, acc=np.float32)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        return 2.0 * 2048 * 2048 * self.K / dt / 1e12, (
+            f"numpy fp32 GEMM 2048x{self.K}x2048 (a 1/64 slice of the job), {n} runs, "
+            f"{threads} BLAS threads")
+
+
+WORKLOADS = {"transpose": TransposeF32, "decoder_stack": DecoderStackDecode,
+             "gemm": ShardedGemm}
 DEFAULT_WORKLOAD = "decoder_stack"
 
 
@@ -456,7 +537,9 @@ def main(argv=None):
         r_unit = "GB/s"
     else:
         achieved = wl.roofline_work() / (launch_ms / 1e3) / 1e12
-        peak = peaks["bf16_tflops"]
+        # a multi-millisecond GEMM runs under the power cap: sustained figure
+        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) \
+            if launch_ms > 2.0 else peaks["bf16_tflops"]
         r_unit = "TFLOP/s"
 
     # ---- end to end through the public API (pinned host in, host out) ------

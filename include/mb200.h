@@ -120,6 +120,12 @@ int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const mb_scalar* s
 int mb_device_status(uint32_t* out);
 int mb_clear_device_status(void);
 
+/* Failure-detection self-test (no counterpart in the reference, whose host
+ * only has die()): one CTA waits on a barrier that never completes, gives up
+ * after timeout_us, records a status bit and returns. Expected result:
+ * MB_ERR_TIMEOUT with the context still usable (clear the status afterwards). */
+int mb_selftest_bounded_wait(int timeout_us, void* stream);
+
 /* ---- transpose_2d (metal/kernels/common/transpose_2d/default.metal:10-48;
  *      hook mlx/kernels/common/transpose_2d.py:10-11) -------------------- */
 

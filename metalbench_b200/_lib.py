@@ -67,6 +67,7 @@ SIGNATURES = {
                          _I, _I, C.POINTER(MbTiming)]),
     "mb_device_status": (C.c_int, [_U32P]),
     "mb_clear_device_status": (C.c_int, []),
+    "mb_selftest_bounded_wait": (C.c_int, [_I, _P]),
     "mb_transpose_2d_f32": (C.c_int, [_P, _P, _I64, _I64, _P]),
     "mb_transpose_batched_bf16": (C.c_int, [_P, _P, _I64, _I64, _I64, _P]),
     "mb_transpose_batched_f32": (C.c_int, [_P, _P, _I64, _I64, _I64, _P]),

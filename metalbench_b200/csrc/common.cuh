@@ -47,6 +47,7 @@ int num_sms();
 #define MB_DEV_TIMEOUT_TMA 0x1u
 #define MB_DEV_TIMEOUT_MMA 0x2u
 #define MB_DEV_TIMEOUT_EPI 0x4u
+#define MB_DEV_TIMEOUT_SELFTEST 0x100u
 
 namespace mbd {
 
@@ -103,14 +104,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // CTA-wide *abort flag when given) if the phase never completes or another
 // role of the CTA already gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
-                                          uint32_t code, volatile int* abort_flag = nullptr) {
+                                          uint32_t code, volatile int* abort_flag = nullptr,
+                                          uint64_t limit_ns = MB_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > MB_WAIT_NS) break;
+      if (globaltimer_ns() - t0 > limit_ns) break;
     }
   }
   if (status) atomicOr(status, code);
