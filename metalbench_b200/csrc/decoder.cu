@@ -85,6 +85,29 @@ __global__ void reduce_sum_kernel(float4* __restrict__ part, int ksplit, int64_t
   part[i] = a;
 }
 
+// Stream-K partials (M <= 128, one tile row): column block t = col / 256 was
+// cut into segments produced by CTAs first..last, first = t*kb/per; segment s
+// of every tile sits in slot s. Sum slots 1.. into slot 0.
+__global__ void reduce_streamk_kernel(float4* __restrict__ part, int M, int N, int kblocks,
+                                      int per) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t n4 = (int64_t)M * N / 4;
+  if (i >= n4) return;
+  const int col = (int)((i * 4) % N);
+  const int t = col / 256;
+  const int first = (int)(((long long)t * kblocks) / per);
+  const int last = (int)(((long long)(t + 1) * kblocks - 1) / per);
+  float4 a = part[i];
+  for (int sgm = 1; sgm <= last - first; ++sgm) {
+    const float4 b = part[sgm * n4 + i];
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+  }
+  part[i] = a;
+}
+
 // Split-K epilogues: one thread per (row, 32-column chunk) of the summed part[0].
 __global__ void reduce_store_kernel(const float* __restrict__ part, int ksplit, int M, int N,
                                     gemm::EpiStore e) {
@@ -178,6 +201,13 @@ int pack(const uint16_t* in, int64_t ld_in, int K, const std::vector<int>& cols,
   return MB_OK;
 }
 
+// Decode-size GEMMs (one tile row, fewer than two tiles per SM) run
+// stream-K: every SM streams the same number of weight k-blocks instead of
+// whole tiles (e.g. 112 gate/up tiles would leave 36 of 148 SMs idle).
+bool use_streamk(int64_t M, int64_t N) {
+  return M <= BM && ((N + 255) / 256) < 2 * mb::num_sms();
+}
+
 int choose_ksplit(int64_t M, int64_t N, int64_t K) {
   const int sms = mb::num_sms();
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + 255) / 256);
@@ -213,6 +243,15 @@ Plan make_plan(const Layer& L, int B, int S, int max_kv_len) {
   auto upd = [&](int ks, int64_t N) {
     if (ks > 1) part = std::max(part, (size_t)ks * T * N * 4);
   };
+  auto upd_sk = [&](int64_t N, int64_t K) {
+    if (!use_streamk(T, N)) return;
+    const StreamK pl = streamk_plan((int)((N + 255) / 256), (int)((K + 63) / 64), mb::num_sms());
+    part = std::max(part, (size_t)pl.max_segs * T * N * 4);
+  };
+  upd_sk(Nqkv, D);
+  upd_sk(D, L.Dq);
+  upd_sk(2 * L.FF, D);
+  upd_sk(D, L.FF);
   upd(p.ks_qkv, Nqkv);
   upd(p.ks_o, D);
   upd(p.ks_gu, 2 * L.FF);
@@ -237,23 +276,36 @@ int gemm_call(const uint16_t* A, const uint16_t* Bw, const Epi& e, int64_t M, in
   return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s);
 }
 
+unsigned blocks_for(int64_t threads);
+
+// Partial sums of A @ Bw^T into part[0] (fp32 [M, N]): stream-K for decode
+// sizes, else split-K with `ks` splits; the splits/segments are summed here.
 int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, int64_t N,
                  int64_t K, int ks, cudaStream_t s) {
   dec::EpiPartial<256> e;
   e.M = (int)M;
   e.N = (int)N;
   e.ws = part;
-  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s);
+  const int64_t n4 = M * N / 4;
+  if (use_streamk(M, N)) {
+    int rc = launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, true);
+    if (rc) return rc;
+    const StreamK pl = streamk_plan((int)((N + 255) / 256), (int)((K + 63) / 64), mb::num_sms());
+    reduce_streamk_kernel<<<blocks_for(n4), 256, 0, s>>>(reinterpret_cast<float4*>(part), (int)M,
+                                                          (int)N, (int)((K + 63) / 64), pl.per);
+  } else {
+    int rc = launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s);
+    if (rc) return rc;
+    if (ks > 1)
+      reduce_sum_kernel<<<blocks_for(n4), 256, 0, s>>>(reinterpret_cast<float4*>(part), ks, n4);
+  }
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
 }
 
 unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
 
-int sum_splits(float* part, int ks, int64_t M, int64_t N, cudaStream_t s) {
-  const int64_t n4 = M * N / 4;
-  reduce_sum_kernel<<<blocks_for(n4), 256, 0, s>>>(reinterpret_cast<float4*>(part), ks, n4);
-  MB_CUDA(cudaGetLastError());
-  return MB_OK;
-}
+
 
 }  // namespace
 
@@ -367,9 +419,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   qp.start_pos = start_pos;
   qp.q_out = q;
   qp.kv = dec::KvCache{k_cache, v_cache, block_table, max_pages, 64};
-  if (p.ks_qkv > 1) {
+  if (p.ks_qkv > 1 || use_streamk(T, Nqkv)) {
     rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s);
-    if (!rc) rc = sum_splits(part, p.ks_qkv, T, Nqkv, s);
     if (rc) return rc;
     reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, 1, (int)T, Nqkv, qp);
   } else {
@@ -401,9 +452,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   eo.alpha = 1.f;
   eo.residual = L.rank == 0 ? x : nullptr;
   eo.ld_res = D;
-  if (p.ks_o > 1) {
+  if (p.ks_o > 1 || use_streamk(T, D)) {
     rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s);
-    if (!rc) rc = sum_splits(part, p.ks_o, T, D, s);
     if (rc) return rc;
     reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, 1, (int)T, D, eo);
   } else {
@@ -426,9 +476,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   sp.FF = L.FF;
   sp.rstd = rstd2;
   sp.act = act;
-  if (p.ks_gu > 1) {
+  if (p.ks_gu > 1 || use_streamk(T, 2 * L.FF)) {
     rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s);
-    if (!rc) rc = sum_splits(part, p.ks_gu, T, 2 * L.FF, s);
     if (rc) return rc;
     reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, 1, (int)T, 2 * L.FF,
                                                                     sp);
@@ -450,9 +499,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   ed.alpha = 1.f;
   ed.residual = L.rank == 0 ? x1 : nullptr;
   ed.ld_res = D;
-  if (p.ks_down > 1) {
+  if (p.ks_down > 1 || use_streamk(T, D)) {
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s);
-    if (!rc) rc = sum_splits(part, p.ks_down, T, D, s);
     if (rc) return rc;
     reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, 1, (int)T, D, ed);
   } else {

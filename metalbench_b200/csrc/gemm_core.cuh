@@ -66,6 +66,45 @@ struct Sched {
     kb0 = ks * kb_per_split;
     kb1 = min(kblocks, kb0 + kb_per_split);
   }
+
+  // Stream-K mode: the (tile, k-block) sequence tile-major is cut into equal
+  // contiguous ranges of sk_per k-blocks, one per CTA, so every SM gets the
+  // same amount of work whatever the tile count. A tile cut by range borders
+  // is computed as several "segments"; segment s of tile t is produced by CTA
+  // floor(t*kblocks/sk_per) + s and the caller sums the segment partials.
+  int streamk = 0;
+  int sk_per = 0;
+
+  struct Cursor {
+    long long pos, end;
+    int t;
+  };
+  __device__ Cursor begin() const {
+    Cursor c;
+    c.t = blockIdx.x;
+    c.pos = (long long)blockIdx.x * sk_per;
+    c.end = streamk ? min(c.pos + sk_per, (long long)tiles_m * tiles_n * kblocks) : 0;
+    return c;
+  }
+  // Next unit of this CTA: tile (tm, tn), segment/split index seg, k-blocks [kb0, kb1).
+  __device__ bool next(Cursor& c, int& tm, int& tn, int& seg, int& kb0, int& kb1) const {
+    if (streamk) {
+      if (c.pos >= c.end) return false;
+      const int tile = (int)(c.pos / kblocks);
+      kb0 = (int)(c.pos % kblocks);
+      kb1 = (int)min((long long)kblocks, kb0 + (c.end - c.pos));
+      int dummy;
+      get(tile, tm, tn, dummy);
+      seg = blockIdx.x - (int)(((long long)tile * kblocks) / sk_per);
+      c.pos += kb1 - kb0;
+      return true;
+    }
+    if (c.t >= total()) return false;
+    get(c.t, tm, tn, seg);
+    krange(seg, kb0, kb1);
+    c.t += gridDim.x;
+    return true;
+  }
 };
 
 // Epilogue context handed to the functor for one tile: the TMEM address of
@@ -198,7 +237,6 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   mbd::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int total = sched.total();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -212,10 +250,9 @@ __global__ void __launch_bounds__(256, 1)
         mbd::mbar_expect_tx(res_full, prod.resident_tx_bytes());
         prod.load_resident(res, res_full);
       }
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        int tm, tn, ks, kb0, kb1;
-        sched.get(t, tm, tn, ks);
-        sched.krange(ks, kb0, kb1);
+      auto cur = sched.begin();
+      int tm, tn, ks, kb0, kb1;
+      while (ok && sched.next(cur, tm, tn, ks, kb0, kb1)) {
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbd::mbar_wait(&empty[stage], phase ^ 1, status, MB_DEV_TIMEOUT_TMA, abort_flag)) {
             ok = false;
@@ -247,10 +284,9 @@ __global__ void __launch_bounds__(256, 1)
         ok = mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_MMA, abort_flag);
       const uint32_t res_u32 = mbd::smem_u32(res);
       int i = 0;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x, ++i) {
-        int tm, tn, ks, kb0, kb1;
-        sched.get(t, tm, tn, ks);
-        sched.krange(ks, kb0, kb1);
+      auto cur = sched.begin();
+      int tm, tn, ks, kb0, kb1;
+      for (; ok && sched.next(cur, tm, tn, ks, kb0, kb1); ++i) {
         const int buf = i & 1;
         const uint32_t tph = (i >> 1) & 1;
         if (!mbd::mbar_wait(&tempty[buf], tph ^ 1, status, MB_DEV_TIMEOUT_MMA, abort_flag)) break;
@@ -279,9 +315,9 @@ __global__ void __launch_bounds__(256, 1)
     // ---------------- epilogue ----------------
     const int q = warp & 3;
     int i = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-      int tm, tn, ks;
-      sched.get(t, tm, tn, ks);
+    auto cur = sched.begin();
+    int tm, tn, ks, kb0, kb1;
+    for (; sched.next(cur, tm, tn, ks, kb0, kb1); ++i) {
       const int buf = i & 1;
       const uint32_t tph = (i >> 1) & 1;
       if (!mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag)) break;

@@ -4,9 +4,25 @@
 
 namespace gemm {
 
+// Stream-K plan for `tiles` output tiles of `kblocks` k-blocks on `sms` CTAs:
+// k-blocks per CTA, CTAs used, and an upper bound on the segments one tile
+// can be cut into (the size of the partial-sum buffer in tiles).
+struct StreamK {
+  int per, ctas, max_segs;
+};
+inline StreamK streamk_plan(int tiles, int kblocks, int sms) {
+  const long long total = (long long)tiles * kblocks;
+  StreamK p;
+  p.per = (int)((total + sms - 1) / sms);
+  if (p.per < 1) p.per = 1;
+  p.ctas = (int)((total + p.per - 1) / p.per);
+  p.max_segs = (kblocks + p.per - 1) / p.per + 1;
+  return p;
+}
+
 template <Mode MODE, int BN, int STAGES, bool B_MN, class Epi>
 inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, int64_t N, int64_t K,
-                int ksplit, cudaStream_t stream) {
+                int ksplit, cudaStream_t stream, bool streamk = false) {
   using P = GemmProducer<MODE, BN, B_MN>;
   using S = Smem<P, BN, STAGES>;
   const int esz = elem_bytes(MODE);
@@ -41,7 +57,15 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
     attr = true;
   }
-  const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
+  int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
+  if (streamk) {
+    const StreamK pl = streamk_plan(sc.tiles_m * sc.tiles_n, sc.kblocks, mb::num_sms());
+    sc.ksplit = 1;
+    sc.kb_per_split = sc.kblocks;
+    sc.streamk = 1;
+    sc.sk_per = pl.per;
+    grid = pl.ctas;
+  }
   kern<<<grid, 256, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
   MB_CUDA(cudaGetLastError());
   return MB_OK;
