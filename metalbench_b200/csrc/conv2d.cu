@@ -35,6 +35,7 @@ struct ConvProducer {
   ConvGeom g;
   static constexpr int KE = 64;
   static constexpr uint32_t BYTES = (BM + BN) * KBYTES;
+  __device__ uint32_t stage_tx_bytes() const { return BYTES; }
   static constexpr int STAGE_BYTES = (BM + BN) * KBYTES;
   static constexpr int RESIDENT_BYTES = 0;
   __device__ uint32_t resident_tx_bytes() const { return 0; }
@@ -85,6 +86,7 @@ struct ConvResProducer {
   static constexpr int MAX_TAPS_CHUNKS = 9;             // KH*KW*cchunks served resident
   static constexpr int RESIDENT_BYTES = MAX_TAPS_CHUNKS * BN * KBYTES;
   static constexpr uint32_t BYTES = STAGE_BYTES;
+  __device__ uint32_t stage_tx_bytes() const { return BYTES; }
   uint32_t resident_tx;  // bytes of the resident weight load
   __device__ uint32_t resident_tx_bytes() const { return resident_tx; }
   __device__ void prefetch() const {

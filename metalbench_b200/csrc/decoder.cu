@@ -51,13 +51,29 @@ __global__ void rownorm_kernel(const uint16_t* __restrict__ x, int M, int D, flo
   if (lane == 0) rstd[row] = rsqrtf(acc / (float)D + eps);
 }
 
-__device__ __forceinline__ void sum_partials(const float* __restrict__ part, int ksplit, int M,
-                                             int N, int row, int col, float (&v)[32]) {
+// How the fp32 partial slots of a column are summed: split-K (per <= 0): the
+// same `slots` splits for every column; stream-K (per > 0): column block
+// col/256 was cut into segments by CTAs first..last (first = t*kblocks/per).
+struct PartSum {
+  int slots;
+  int kblocks, per;
+  int64_t stride;  // elements per slot (M * N)
+  __device__ int count(int col) const {
+    if (per <= 0) return slots;
+    const int t = col / 256;
+    const int first = (int)(((long long)t * kblocks) / per);
+    const int last = (int)(((long long)(t + 1) * kblocks - 1) / per);
+    return last - first + 1;
+  }
+};
+
+__device__ __forceinline__ void sum_slots(const float* __restrict__ part, const PartSum& ps, int N,
+                                          int row, int col, float (&v)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = 0.f;
-  for (int k = 0; k < ksplit; ++k) {
-    const float4* p =
-        reinterpret_cast<const float4*>(part + ((int64_t)k * M + row) * N + col);
+  const int n = ps.count(col);
+  for (int k = 0; k < n; ++k) {
+    const float4* p = reinterpret_cast<const float4*>(part + k * ps.stride + (int64_t)row * N + col);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 t = p[j];
@@ -69,54 +85,25 @@ __device__ __forceinline__ void sum_partials(const float* __restrict__ part, int
   }
 }
 
-// part[0] += part[1..ksplit-1], four floats per thread (wide, so the sum is
-// bandwidth- not latency-bound); the epilogue kernels then read part[0] only.
-__global__ void reduce_sum_kernel(float4* __restrict__ part, int ksplit, int64_t n4) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  float4 a = part[i];
-  for (int k = 1; k < ksplit; ++k) {
-    const float4 t = part[k * n4 + i];
-    a.x += t.x;
-    a.y += t.y;
-    a.z += t.z;
-    a.w += t.w;
+// Split-K / stream-K epilogue: out = scale * sum + residual, one thread per
+// (row, 32-column chunk). With rstd_out, the grid is one CTA per row (N/32
+// threads) and the CTA also writes rstd_out[row] = rsqrt(mean(out^2) + eps)
+// of the bf16 values it stored: the next RMSNorm without another pass.
+__global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
+                                    gemm::EpiStore e, float* __restrict__ rstd_out, float eps) {
+  int row, col;
+  if (rstd_out) {
+    row = blockIdx.x;
+    col = threadIdx.x * 32;
+  } else {
+    const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int chunks = N / 32;
+    if (t >= (int64_t)M * chunks) return;
+    row = (int)(t / chunks);
+    col = (int)(t % chunks) * 32;
   }
-  part[i] = a;
-}
-
-// Stream-K partials (M <= 128, one tile row): column block t = col / 256 was
-// cut into segments produced by CTAs first..last, first = t*kb/per; segment s
-// of every tile sits in slot s. Sum slots 1.. into slot 0.
-__global__ void reduce_streamk_kernel(float4* __restrict__ part, int M, int N, int kblocks,
-                                      int per) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t n4 = (int64_t)M * N / 4;
-  if (i >= n4) return;
-  const int col = (int)((i * 4) % N);
-  const int t = col / 256;
-  const int first = (int)(((long long)t * kblocks) / per);
-  const int last = (int)(((long long)(t + 1) * kblocks - 1) / per);
-  float4 a = part[i];
-  for (int sgm = 1; sgm <= last - first; ++sgm) {
-    const float4 b = part[sgm * n4 + i];
-    a.x += b.x;
-    a.y += b.y;
-    a.z += b.z;
-    a.w += b.w;
-  }
-  part[i] = a;
-}
-
-// Split-K epilogues: one thread per (row, 32-column chunk) of the summed part[0].
-__global__ void reduce_store_kernel(const float* __restrict__ part, int ksplit, int M, int N,
-                                    gemm::EpiStore e) {
-  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int chunks = N / 32;
-  if (t >= (int64_t)M * chunks) return;
-  const int row = (int)(t / chunks), col = (int)(t % chunks) * 32;
   float v[32];
-  sum_partials(part, ksplit, M, N, row, col, v);
+  sum_slots(part, ps, N, row, col, v);
   const float sc = e.row_scale ? e.row_scale[row] * e.alpha : e.alpha;
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] *= sc;
@@ -126,21 +113,39 @@ __global__ void reduce_store_kernel(const float* __restrict__ part, int ksplit, 
     for (int j = 0; j < 32; ++j) v[j] += gemm::bf16_bits_to_f32(r[j]);
   }
   gemm::store_row32(e.out, e.ldo, e.out_f32, row, col, e.N, v);
+  if (!rstd_out) return;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float q = __bfloat162float(__float2bfloat16_rn(v[j]));  // the stored value
+    ss += q * q;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  __shared__ float wsum[32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) wsum[w] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) t += wsum[i];
+    rstd_out[row] = rsqrtf(t / (float)N + eps);
+  }
 }
 
-__global__ void reduce_qkv_kernel(const float* __restrict__ part, int ksplit, int M, int N,
+__global__ void reduce_qkv_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                   dec::QkvParams qp) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int chunks = N / 32;
   if (t >= (int64_t)M * chunks) return;
   const int row = (int)(t / chunks), col = (int)(t % chunks) * 32;
   float v[32];
-  sum_partials(part, ksplit, M, N, row, col, v);
+  sum_slots(part, ps, N, row, col, v);
   qp.apply(row, col, v);
 }
 
 // N = 2*FF packed columns; thread per (row, 32 output features).
-__global__ void reduce_swiglu_kernel(const float* __restrict__ part, int ksplit, int M, int N,
+__global__ void reduce_swiglu_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                      dec::SwigluParams sp) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int chunks = sp.FF / 32;
@@ -148,8 +153,8 @@ __global__ void reduce_swiglu_kernel(const float* __restrict__ part, int ksplit,
   const int row = (int)(t / chunks), f = (int)(t % chunks) * 32;
   const int gcol = (f / 128) * 256 + f % 128;
   float g[32], u[32];
-  sum_partials(part, ksplit, M, N, row, gcol, g);
-  sum_partials(part, ksplit, M, N, row, gcol + 128, u);
+  sum_slots(part, ps, N, row, gcol, g);
+  sum_slots(part, ps, N, row, gcol + 128, u);
   sp.apply(row, f, g, u);
 }
 
@@ -276,31 +281,26 @@ int gemm_call(const uint16_t* A, const uint16_t* Bw, const Epi& e, int64_t M, in
   return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s);
 }
 
-unsigned blocks_for(int64_t threads);
-
-// Partial sums of A @ Bw^T into part[0] (fp32 [M, N]): stream-K for decode
-// sizes, else split-K with `ks` splits; the splits/segments are summed here.
+// Partial sums of A @ Bw^T into fp32 slots of part ([slot][M][N]): stream-K
+// for decode sizes, else split-K with `ks` splits. *ps tells the epilogue
+// kernels how many slots each column sums.
 int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, int64_t N,
-                 int64_t K, int ks, cudaStream_t s) {
+                 int64_t K, int ks, cudaStream_t s, PartSum* ps) {
   dec::EpiPartial<256> e;
   e.M = (int)M;
   e.N = (int)N;
   e.ws = part;
-  const int64_t n4 = M * N / 4;
+  ps->stride = M * N;
+  ps->kblocks = (int)((K + 63) / 64);
   if (use_streamk(M, N)) {
-    int rc = launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, true);
-    if (rc) return rc;
-    const StreamK pl = streamk_plan((int)((N + 255) / 256), (int)((K + 63) / 64), mb::num_sms());
-    reduce_streamk_kernel<<<blocks_for(n4), 256, 0, s>>>(reinterpret_cast<float4*>(part), (int)M,
-                                                          (int)N, (int)((K + 63) / 64), pl.per);
-  } else {
-    int rc = launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s);
-    if (rc) return rc;
-    if (ks > 1)
-      reduce_sum_kernel<<<blocks_for(n4), 256, 0, s>>>(reinterpret_cast<float4*>(part), ks, n4);
+    const StreamK pl = streamk_plan((int)((N + 255) / 256), ps->kblocks, mb::num_sms());
+    ps->per = pl.per;
+    ps->slots = 0;
+    return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, true);
   }
-  MB_CUDA(cudaGetLastError());
-  return MB_OK;
+  ps->per = 0;
+  ps->slots = ks;
+  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s);
 }
 
 unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
@@ -420,9 +420,10 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   qp.q_out = q;
   qp.kv = dec::KvCache{k_cache, v_cache, block_table, max_pages, 64};
   if (p.ks_qkv > 1 || use_streamk(T, Nqkv)) {
-    rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s);
+    PartSum ps;
+    rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s, &ps);
     if (rc) return rc;
-    reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, 1, (int)T, Nqkv, qp);
+    reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, ps, (int)T, Nqkv, qp);
   } else {
     dec::EpiQKV<256> e;
     e.M = (int)T;
@@ -443,6 +444,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
                                    kv_len, B, S, L.Hq, L.Hkv, Dh, causal, attn, L.Dq, s);
   if (rc) return rc;
 
+  bool rstd2_done = false;
   // 4. x1 = x + attn @ Wo (rank 0 adds the residual; the all-reduce sums shards)
   EpiStore eo{};
   eo.M = (int)T;
@@ -453,9 +455,17 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   eo.residual = L.rank == 0 ? x : nullptr;
   eo.ld_res = D;
   if (p.ks_o > 1 || use_streamk(T, D)) {
-    rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s);
+    PartSum ps;
+    rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s, &ps);
     if (rc) return rc;
-    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, 1, (int)T, D, eo);
+    if (L.world == 1 && D / 32 <= 1024) {  // the reduce also yields rstd2 (one CTA per row)
+      reduce_store_kernel<<<(unsigned)T, D / 32, 0, s>>>(part, ps, (int)T, D, eo, rstd2,
+                                                         L.cfg.eps);
+      rstd2_done = true;
+    } else {
+      reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, ps, (int)T, D, eo, nullptr,
+                                                                 0.f);
+    }
   } else {
     Epi<256, EpiStore> e{};
     static_cast<EpiStore&>(e) = eo;
@@ -468,18 +478,21 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     if (rc) return rc;
   }
 
-  // 5. rstd2, 6. SwiGLU MLP up
-  rownorm_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(x1, (int)T, D, L.cfg.eps, rstd2);
-  MB_CUDA(cudaGetLastError());
+  // 5. rstd2 (unless the o-proj reduce produced it), 6. SwiGLU MLP up
+  if (!rstd2_done) {
+    rownorm_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(x1, (int)T, D, L.cfg.eps, rstd2);
+    MB_CUDA(cudaGetLastError());
+  }
   dec::SwigluParams sp;
   sp.M = (int)T;
   sp.FF = L.FF;
   sp.rstd = rstd2;
   sp.act = act;
   if (p.ks_gu > 1 || use_streamk(T, 2 * L.FF)) {
-    rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s);
+    PartSum ps;
+    rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s, &ps);
     if (rc) return rc;
-    reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, 1, (int)T, 2 * L.FF,
+    reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, ps, (int)T, 2 * L.FF,
                                                                     sp);
   } else {
     dec::EpiSwiGLU e;
@@ -500,9 +513,11 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   ed.residual = L.rank == 0 ? x1 : nullptr;
   ed.ld_res = D;
   if (p.ks_down > 1 || use_streamk(T, D)) {
-    rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s);
+    PartSum ps;
+    rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s, &ps);
     if (rc) return rc;
-    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, 1, (int)T, D, ed);
+    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, ps, (int)T, D, ed, nullptr,
+                                                               0.f);
   } else {
     Epi<256, EpiStore> e{};
     static_cast<EpiStore&>(e) = ed;

@@ -129,6 +129,11 @@ struct EpiCtx {
 template <Mode MODE, int BN, bool B_MN>
 struct GemmProducer {
   CUtensorMap a, b, alo, blo;  // alo / blo: TF32x3 remainders (K-major)
+  // Rows of A one stage actually loads (the A box height): BM, or the row count
+  // rounded up to 16 when M < BM (decode). Rows past it keep stale shared data
+  // that only reaches accumulator rows >= M, which no epilogue stores.
+  uint32_t a_rows = BM;
+  __device__ uint32_t stage_tx_bytes() const { return PARTS * (a_rows + BN) * KBYTES; }
   static constexpr int KE = KBYTES / elem_bytes(MODE);  // K elements per stage
   static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;
   static constexpr uint32_t BYTES = PARTS * (BM + BN) * KBYTES;
@@ -258,7 +263,7 @@ __global__ void __launch_bounds__(256, 1)
             ok = false;
             break;
           }
-          mbd::mbar_expect_tx(&full[stage], Producer::BYTES);
+          mbd::mbar_expect_tx(&full[stage], prod.stage_tx_bytes());
           prod.load(sA(stage), &full[stage], tm, tn, kb);
           issued = (issued & ~(1u << stage)) | (phase << stage);
           used |= 1u << stage;

@@ -34,7 +34,8 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
              "gemm: operands must be 16-byte aligned");
   MB_REQUIRE(!B_MN || (N * esz) % 16 == 0, "gemm: N*elem_size must be a multiple of 16 bytes");
   P p;
-  int rc = mb::make_tmap_2d(&p.a, A, dt, esz, K, M, K * esz, P::KE, BM,
+  p.a_rows = M < BM ? (uint32_t)((M + 15) / 16 * 16) : (uint32_t)BM;
+  int rc = mb::make_tmap_2d(&p.a, A, dt, esz, K, M, K * esz, P::KE, p.a_rows,
                             CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (!B_MN)
