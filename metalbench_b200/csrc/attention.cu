@@ -79,6 +79,19 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Four 8x8 b16 matrices from shared memory; lane l gives the address of row
+// l%8 of matrix l/8. Padded 272-byte rows put the 8 rows on distinct banks.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(mbd::smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(mbd::smem_u32(p)));
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -162,12 +175,14 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const uint16_t* kr = K + (nt * 8 + gid) * KV_LD + tig * 2;
+      // matrices (keys nt*8.., dims ks*16 + {0,8,16,24}): b0, b1 of k-steps ks, ks+1
+      const uint16_t* kr = K + (nt * 8 + (lane & 7)) * KV_LD + (lane >> 3) * 8;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + ks * 16);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8);
-        mma_bf16_16816(s[nt], qa[ks], b0, b1);
+      for (int ks = 0; ks < 8; ks += 2) {
+        uint32_t b[4];
+        ldsm_x4(b, kr + ks * 16);
+        mma_bf16_16816(s[nt], qa[ks], b[0], b[1]);
+        mma_bf16_16816(s[nt], qa[ks + 1], b[2], b[3]);
       }
     }
     // mask + scale, row max
@@ -223,13 +238,15 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(
       pa[1] = pack2(s[2 * k2][2], s[2 * k2][3]);
       pa[2] = pack2(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
       pa[3] = pack2(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
-      const uint16_t* v0 = V + (k2 * 16 + tig * 2) * KV_LD + gid;
+      // transposed matrices (keys k2*16 + {0,8}, dims dt*8 + {0,8}): b0, b1 of dt, dt+1
+      const uint16_t* vr =
+          V + (k2 * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * KV_LD + (lane >> 4) * 8;
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt) {
-        const uint16_t* vp = v0 + dt * 8;
-        const uint32_t b0 = (uint32_t)vp[0] | ((uint32_t)vp[KV_LD] << 16);
-        const uint32_t b1 = (uint32_t)vp[8 * KV_LD] | ((uint32_t)vp[9 * KV_LD] << 16);
-        mma_bf16_16816(o[dt], pa, b0, b1);
+      for (int dt = 0; dt < 16; dt += 2) {
+        uint32_t b[4];
+        ldsm_x4_t(b, vr + dt * 8);
+        mma_bf16_16816(o[dt], pa, b[0], b[1]);
+        mma_bf16_16816(o[dt + 1], pa, b[2], b[3]);
       }
     }
     __syncthreads();  // the buffer is refilled two iterations later
@@ -331,11 +348,14 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const uint16_t* kr = K + (nt * 8 + gid) * KV_LD + tig * 2;
+      const uint16_t* kr = K + (nt * 8 + (lane & 7)) * KV_LD + (lane >> 3) * 8;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        mma_bf16_16816(s[nt], qa[ks], *reinterpret_cast<const uint32_t*>(kr + ks * 16),
-                       *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8));
+      for (int ks = 0; ks < 8; ks += 2) {
+        uint32_t b[4];
+        ldsm_x4(b, kr + ks * 16);
+        mma_bf16_16816(s[nt], qa[ks], b[0], b[1]);
+        mma_bf16_16816(s[nt], qa[ks + 1], b[2], b[3]);
+      }
     }
     float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
@@ -375,17 +395,21 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
     pa[1] = pack2(s[0][2], s[0][3]);
     pa[2] = pack2(s[1][0], s[1][1]);
     pa[3] = pack2(s[1][2], s[1][3]);
-    const uint16_t* v0 = V + (tig * 2) * KV_LD + gid;
+    const uint16_t* vr = V + (((lane >> 3) & 1) * 8 + (lane & 7)) * KV_LD + (lane >> 4) * 8;
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
+    for (int dt = 0; dt < 16; dt += 2) {
       o[dt][0] *= ca;
       o[dt][1] *= ca;
       o[dt][2] *= cb;
       o[dt][3] *= cb;
-      const uint16_t* vp = v0 + dt * 8;
-      const uint32_t b0 = (uint32_t)vp[0] | ((uint32_t)vp[KV_LD] << 16);
-      const uint32_t b1 = (uint32_t)vp[8 * KV_LD] | ((uint32_t)vp[9 * KV_LD] << 16);
-      mma_bf16_16816(o[dt], pa, b0, b1);
+      o[dt + 1][0] *= ca;
+      o[dt + 1][1] *= ca;
+      o[dt + 1][2] *= cb;
+      o[dt + 1][3] *= cb;
+      uint32_t b[4];
+      ldsm_x4_t(b, vr + dt * 8);
+      mma_bf16_16816(o[dt], pa, b[0], b[1]);
+      mma_bf16_16816(o[dt + 1], pa, b[2], b[3]);
     }
     __syncthreads();  // this buffer is refilled STAGES-1 iterations later
   }

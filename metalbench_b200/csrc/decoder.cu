@@ -72,16 +72,25 @@ __device__ __forceinline__ void sum_slots(const float* __restrict__ part, const 
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = 0.f;
   const int n = ps.count(col);
-  for (int k = 0; k < n; ++k) {
-    const float4* p = reinterpret_cast<const float4*>(part + k * ps.stride + (int64_t)row * N + col);
+  for (int k0 = 0; k0 < n; k0 += 4) {
+    // up to four slots' loads in flight before any add
+    float4 t[4][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 t = p[j];
-      v[4 * j] += t.x;
-      v[4 * j + 1] += t.y;
-      v[4 * j + 2] += t.z;
-      v[4 * j + 3] += t.w;
+    for (int k = 0; k < 4; ++k) {
+      const float4* p =
+          reinterpret_cast<const float4*>(part + (k0 + k) * ps.stride + (int64_t)row * N + col);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[k][j] = k0 + k < n ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += t[k][j].x;
+        v[4 * j + 1] += t[k][j].y;
+        v[4 * j + 2] += t[k][j].z;
+        v[4 * j + 3] += t[k][j].w;
+      }
   }
 }
 
@@ -296,6 +305,7 @@ int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, 
     const StreamK pl = streamk_plan((int)((N + 255) / 256), ps->kblocks, mb::num_sms());
     ps->per = pl.per;
     ps->slots = 0;
+    if (M <= 64) return launch_gemm_decode<256, 5>(A, Bw, e, M, N, K, s);
     return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, true);
   }
   ps->per = 0;

@@ -201,6 +201,40 @@ struct GemmProducer {
   }
 };
 
+// Decode-size producer (bf16, both operands K-major): A, the activations, has
+// at most AROWS rows, so a stage holds an AROWS-row A box followed by the
+// BN-row weight box, and the ring can be deeper than with 128-row A tiles.
+// The MMA still reads 128 A rows; rows AROWS..127 alias the start of the B box
+// and only reach accumulator rows >= M, which no epilogue stores.
+template <int BN, int AROWS>
+struct DecodeProducer {
+  CUtensorMap a, b;
+  static constexpr int KE = 64;
+  static constexpr int STAGE_BYTES = (AROWS + BN) * KBYTES;
+  static constexpr int RESIDENT_BYTES = 0;
+  static_assert((AROWS * KBYTES) % 1024 == 0, "B box must stay swizzle-atom aligned");
+  uint32_t a_rows;  // <= AROWS, multiple of 16
+  __device__ uint32_t stage_tx_bytes() const { return (a_rows + BN) * KBYTES; }
+  __device__ uint32_t resident_tx_bytes() const { return 0; }
+  __device__ void prefetch() const {
+    mbd::prefetch_tmap(&a);
+    mbd::prefetch_tmap(&b);
+  }
+  __device__ void load_resident(uint8_t*, uint64_t*) const {}
+  __device__ void load(uint8_t* st, uint64_t* bar, int tm, int tn, int kb) const {
+    mbd::tma_load_2d(st, &a, bar, kb * KE, tm * BM);
+    mbd::tma_load_2d(st + AROWS * KBYTES, &b, bar, kb * KE, tn * BN);
+  }
+  __device__ void issue(uint32_t d, uint32_t st, uint32_t, int, bool first) const {
+    constexpr uint32_t idesc = mbd::make_idesc(1u, BM, BN, 0, 0);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      mbd::mma_f16(d, mbd::sw128_desc(st + kk * 32, 16, 1024),
+                   mbd::sw128_desc(st + AROWS * KBYTES + kk * 32, 16, 1024), idesc,
+                   (!first || kk > 0) ? 1u : 0u);
+  }
+};
+
 template <int BN, int STAGES, class Producer, class Epi>
 __global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ Producer prod, const __grid_constant__ Epi epi,

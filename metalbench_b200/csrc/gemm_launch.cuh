@@ -73,4 +73,41 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
 }
 
 
+// Stream-K GEMM for decode sizes (M <= 64): bf16, B K-major [N, K].
+template <int BN, int STAGES, class Epi>
+inline int launch_gemm_decode(const void* A, const void* B, const Epi& epi, int64_t M, int64_t N,
+                              int64_t K, cudaStream_t stream) {
+  using P = DecodeProducer<BN, 64>;
+  using S = Smem<P, BN, STAGES>;
+  static_assert(S::TOTAL <= 232448, "decode GEMM: shared memory over the sm_100 limit");
+  MB_REQUIRE(M >= 1 && M <= 64, "decode GEMM: M must be in [1, 64]");
+  MB_REQUIRE(K % 8 == 0, "decode GEMM: K must be a multiple of 8");
+  P p;
+  p.a_rows = (uint32_t)((M + 15) / 16 * 16);
+  int rc = mb::make_tmap_2d(&p.a, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, K * 2, 64,
+                            p.a_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = mb::make_tmap_2d(&p.b, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, K * 2, 64, BN,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  Sched sc;
+  sc.tiles_m = 1;
+  sc.tiles_n = (int)((N + BN - 1) / BN);
+  sc.kblocks = (int)((K + 63) / 64);
+  sc.ksplit = 1;
+  sc.kb_per_split = sc.kblocks;
+  const StreamK pl = streamk_plan(sc.tiles_n, sc.kblocks, mb::num_sms());
+  sc.streamk = 1;
+  sc.sk_per = pl.per;
+  auto kern = gemm_kernel<BN, STAGES, P, Epi>;
+  static bool attr = false;
+  if (!attr) {
+    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr = true;
+  }
+  kern<<<pl.ctas, 256, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
 }  // namespace gemm
