@@ -67,25 +67,27 @@ struct PartSum {
   }
 };
 
+constexpr int RW = 8;  // columns per thread in the reduce kernels (16-byte bf16 stores)
+
 __device__ __forceinline__ void sum_slots(const float* __restrict__ part, const PartSum& ps, int N,
-                                          int row, int col, float (&v)[32]) {
+                                          int row, int col, float (&v)[RW]) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  for (int j = 0; j < RW; ++j) v[j] = 0.f;
   const int n = ps.count(col);
   for (int k0 = 0; k0 < n; k0 += 4) {
-    // up to four slots' loads in flight before any add
-    float4 t[4][8];
+    float4 t[4][RW / 4];  // up to four slots' loads in flight before any add
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float4* p =
           reinterpret_cast<const float4*>(part + (k0 + k) * ps.stride + (int64_t)row * N + col);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) t[k][j] = k0 + k < n ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < RW / 4; ++j)
+        t[k][j] = k0 + k < n ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < RW / 4; ++j) {
         v[4 * j] += t[k][j].x;
         v[4 * j + 1] += t[k][j].y;
         v[4 * j + 2] += t[k][j].z;
@@ -95,37 +97,41 @@ __device__ __forceinline__ void sum_slots(const float* __restrict__ part, const 
 }
 
 // Split-K / stream-K epilogue: out = scale * sum + residual, one thread per
-// (row, 32-column chunk). With rstd_out, the grid is one CTA per row (N/32
-// threads) and the CTA also writes rstd_out[row] = rsqrt(mean(out^2) + eps)
-// of the bf16 values it stored: the next RMSNorm without another pass.
+// (row, 8 columns). With rstd_out, the grid is one CTA per row (N/8 threads)
+// and the CTA also writes rstd_out[row] = rsqrt(mean(out^2) + eps) of the
+// bf16 values it stored: the next RMSNorm without another pass.
 __global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                     gemm::EpiStore e, float* __restrict__ rstd_out, float eps) {
   int row, col;
   if (rstd_out) {
     row = blockIdx.x;
-    col = threadIdx.x * 32;
+    col = threadIdx.x * RW;
   } else {
     const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    const int chunks = N / 32;
+    const int chunks = N / RW;
     if (t >= (int64_t)M * chunks) return;
     row = (int)(t / chunks);
-    col = (int)(t % chunks) * 32;
+    col = (int)(t % chunks) * RW;
   }
-  float v[32];
+  float v[RW];
   sum_slots(part, ps, N, row, col, v);
   const float sc = e.row_scale ? e.row_scale[row] * e.alpha : e.alpha;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] *= sc;
+  for (int j = 0; j < RW; ++j) v[j] *= sc;
   if (e.residual) {
-    const uint16_t* r = e.residual + (int64_t)row * e.ld_res + col;
+    const uint4 w = *reinterpret_cast<const uint4*>(e.residual + (int64_t)row * e.ld_res + col);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += gemm::bf16_bits_to_f32(r[j]);
+    for (int m = 0; m < 4; ++m) {
+      v[2 * m] += __uint_as_float(ws[m] << 16);
+      v[2 * m + 1] += __uint_as_float(ws[m] & 0xFFFF0000u);
+    }
   }
-  gemm::store_row32(e.out, e.ldo, e.out_f32, row, col, e.N, v);
+  gemm::store_rowW<RW>(e.out, e.ldo, e.out_f32, row, col, e.N, v);
   if (!rstd_out) return;
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
+  for (int j = 0; j < RW; ++j) {
     const float q = __bfloat162float(__float2bfloat16_rn(v[j]));  // the stored value
     ss += q * q;
   }
@@ -145,26 +151,26 @@ __global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, 
 __global__ void reduce_qkv_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                   dec::QkvParams qp) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int chunks = N / 32;
+  const int chunks = N / RW;
   if (t >= (int64_t)M * chunks) return;
-  const int row = (int)(t / chunks), col = (int)(t % chunks) * 32;
-  float v[32];
+  const int row = (int)(t / chunks), col = (int)(t % chunks) * RW;
+  float v[RW];
   sum_slots(part, ps, N, row, col, v);
-  qp.apply(row, col, v);
+  qp.apply<RW>(row, col, v);
 }
 
-// N = 2*FF packed columns; thread per (row, 32 output features).
+// N = 2*FF packed columns; thread per (row, 8 output features).
 __global__ void reduce_swiglu_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                      dec::SwigluParams sp) {
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int chunks = sp.FF / 32;
+  const int chunks = sp.FF / RW;
   if (t >= (int64_t)M * chunks) return;
-  const int row = (int)(t / chunks), f = (int)(t % chunks) * 32;
+  const int row = (int)(t / chunks), f = (int)(t % chunks) * RW;
   const int gcol = (f / 128) * 256 + f % 128;
-  float g[32], u[32];
+  float g[RW], u[RW];
   sum_slots(part, ps, N, row, gcol, g);
   sum_slots(part, ps, N, row, gcol + 128, u);
-  sp.apply(row, f, g, u);
+  sp.apply<RW>(row, f, g, u);
 }
 
 // out[n][k] = in[k * ld_in + col_idx[n]] for k < K: packs selected columns of a
@@ -433,7 +439,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s, &ps);
     if (rc) return rc;
-    reduce_qkv_kernel<<<blocks_for(T * Nqkv / 32), 256, 0, s>>>(part, ps, (int)T, Nqkv, qp);
+    reduce_qkv_kernel<<<blocks_for(T * Nqkv / RW), 256, 0, s>>>(part, ps, (int)T, Nqkv, qp);
   } else {
     dec::EpiQKV<256> e;
     e.M = (int)T;
@@ -468,12 +474,12 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s, &ps);
     if (rc) return rc;
-    if (L.world == 1 && D / 32 <= 1024) {  // the reduce also yields rstd2 (one CTA per row)
-      reduce_store_kernel<<<(unsigned)T, D / 32, 0, s>>>(part, ps, (int)T, D, eo, rstd2,
+    if (L.world == 1 && D / RW <= 1024) {  // the reduce also yields rstd2 (one CTA per row)
+      reduce_store_kernel<<<(unsigned)T, D / RW, 0, s>>>(part, ps, (int)T, D, eo, rstd2,
                                                          L.cfg.eps);
       rstd2_done = true;
     } else {
-      reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, ps, (int)T, D, eo, nullptr,
+      reduce_store_kernel<<<blocks_for(T * D / RW), 256, 0, s>>>(part, ps, (int)T, D, eo, nullptr,
                                                                  0.f);
     }
   } else {
@@ -502,7 +508,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s, &ps);
     if (rc) return rc;
-    reduce_swiglu_kernel<<<blocks_for(T * L.FF / 32), 256, 0, s>>>(part, ps, (int)T, 2 * L.FF,
+    reduce_swiglu_kernel<<<blocks_for(T * L.FF / RW), 256, 0, s>>>(part, ps, (int)T, 2 * L.FF,
                                                                     sp);
   } else {
     dec::EpiSwiGLU e;
@@ -526,7 +532,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s, &ps);
     if (rc) return rc;
-    reduce_store_kernel<<<blocks_for(T * D / 32), 256, 0, s>>>(part, ps, (int)T, D, ed, nullptr,
+    reduce_store_kernel<<<blocks_for(T * D / RW), 256, 0, s>>>(part, ps, (int)T, D, ed, nullptr,
                                                                0.f);
   } else {
     Epi<256, EpiStore> e{};

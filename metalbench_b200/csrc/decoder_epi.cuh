@@ -38,10 +38,11 @@ struct QkvParams {
   uint16_t* q_out;                // [M, Hq*Dh]
   KvCache kv;
 
-  // Rotate adjacent pairs (2i, 2i+1) of head-local dims d0..d0+31.
-  __device__ __forceinline__ void rope32(float (&v)[32], int pos, int d0) const {
+  // Rotate adjacent pairs (2i, 2i+1) of head-local dims d0..d0+W-1.
+  template <int W>
+  __device__ __forceinline__ void rope(float (&v)[W], int pos, int d0) const {
 #pragma unroll
-    for (int j = 0; j < 32; j += 2) {
+    for (int j = 0; j < W; j += 2) {
       const int i = (d0 + j) >> 1;
       const float inv_freq = exp2f(neg_log2_base_over_half * (float)i);
       float sn, cs;
@@ -52,25 +53,26 @@ struct QkvParams {
     }
   }
 
-  __device__ void apply(int row, int col, float (&v)[32]) const {
+  template <int W>
+  __device__ void apply(int row, int col, float (&v)[W]) const {
     const float sc = rstd ? rstd[row] : 1.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= sc;
+    for (int j = 0; j < W; ++j) v[j] *= sc;
     const int b = row / S, s = row % S;
     const int pos = start_pos[b] + s;
     const int Dq = Hq * Dh, Dk = Hkv * Dh;
     if (col < Dq) {
-      rope32(v, pos, col % Dh);
-      gemm::store_row32(q_out, Dq, 0, row, col, Dq, v);
+      rope<W>(v, pos, col % Dh);
+      gemm::store_rowW<W>(q_out, Dq, 0, row, col, Dq, v);
       return;
     }
     const bool is_k = col < Dq + Dk;
     const int c = is_k ? col - Dq : col - Dq - Dk;
     const int head = c / Dh, d = c % Dh;
-    if (is_k) rope32(v, pos, d);
+    if (is_k) rope<W>(v, pos, d);
     const int pg = kv.block_table[b * kv.max_pages + pos / kv.page];
     const int64_t off = (((int64_t)pg * Hkv + head) * kv.page + pos % kv.page) * Dh + d;
-    gemm::store32_bf16((is_k ? kv.k : kv.v) + off, v);
+    gemm::storeW_bf16<W>((is_k ? kv.k : kv.v) + off, v);
   }
 };
 
@@ -81,14 +83,15 @@ struct SwigluParams {
   int M, FF;
   const float* rstd;
   uint16_t* act;  // [M, FF]
-  __device__ void apply(int row, int f, float (&g)[32], const float (&u)[32]) const {
+  template <int W>
+  __device__ void apply(int row, int f, float (&g)[W], const float (&u)[W]) const {
     const float sc = rstd ? rstd[row] : 1.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < W; ++j) {
       const float a = g[j] * sc, b = u[j] * sc;
       g[j] = a / (1.f + __expf(-a)) * b;
     }
-    gemm::store_row32(act, FF, 0, row, f, FF, g);
+    gemm::store_rowW<W>(act, FF, 0, row, f, FF, g);
   }
 };
 

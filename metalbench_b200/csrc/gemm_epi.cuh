@@ -28,25 +28,27 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }
 
-// Store 32 consecutive values of one row: vectorised when fully in range.
-__device__ __forceinline__ void store_row32(void* out, int64_t ldo, int out_f32, int row, int n,
-                                            int N, const float (&v)[32]) {
+// Store W consecutive values of one row (bf16 or fp32): vectorised when fully
+// in range and 16-byte aligned, element-wise with bounds checks otherwise.
+template <int W>
+__device__ __forceinline__ void store_rowW(void* out, int64_t ldo, int out_f32, int row, int n,
+                                           int N, const float (&v)[W]) {
   if (out_f32) {
     float* p = reinterpret_cast<float*>(out) + (int64_t)row * ldo + n;
-    if (n + 32 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    if (n + W <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4)
+      for (int j = 0; j < W; j += 4)
         *reinterpret_cast<float4*>(p + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int j = 0; j < W; ++j)
         if (n + j < N) p[j] = v[j];
     }
   } else {
     uint16_t* p = reinterpret_cast<uint16_t*>(out) + (int64_t)row * ldo + n;
-    if (n + 32 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    if (n + W <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
+      for (int j = 0; j < W; j += 8) {
         uint4 w;
         w.x = pack_bf16(v[j], v[j + 1]);
         w.y = pack_bf16(v[j + 2], v[j + 3]);
@@ -56,7 +58,7 @@ __device__ __forceinline__ void store_row32(void* out, int64_t ldo, int out_f32,
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int j = 0; j < W; ++j)
         if (n + j < N) {
           __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
           p[j] = *reinterpret_cast<uint16_t*>(&h);
@@ -65,11 +67,17 @@ __device__ __forceinline__ void store_row32(void* out, int64_t ldo, int out_f32,
   }
 }
 
-// 32 bf16 values to p (vectorised when 16-byte aligned).
-__device__ __forceinline__ void store32_bf16(uint16_t* p, const float (&v)[32]) {
+__device__ __forceinline__ void store_row32(void* out, int64_t ldo, int out_f32, int row, int n,
+                                            int N, const float (&v)[32]) {
+  store_rowW<32>(out, ldo, out_f32, row, n, N, v);
+}
+
+// W bf16 values to p (vectorised when 16-byte aligned).
+template <int W>
+__device__ __forceinline__ void storeW_bf16(uint16_t* p, const float (&v)[W]) {
   if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
+    for (int j = 0; j < W; j += 8) {
       uint4 w;
       w.x = pack_bf16(v[j], v[j + 1]);
       w.y = pack_bf16(v[j + 2], v[j + 3]);
@@ -79,7 +87,7 @@ __device__ __forceinline__ void store32_bf16(uint16_t* p, const float (&v)[32]) 
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < W; ++j) {
       __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
       p[j] = *reinterpret_cast<uint16_t*>(&h);
     }
