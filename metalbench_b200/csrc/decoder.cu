@@ -173,6 +173,26 @@ __global__ void reduce_swiglu_kernel(const float* __restrict__ part, PartSum ps,
   sp.apply<RW>(row, f, g, u);
 }
 
+// Tile a K-major bf16 [N, K] weight for bulk-copy streaming (layout: see
+// tiled_weight_bytes in gemm_launch.cuh).
+__global__ void tile_weights_kernel(const uint16_t* __restrict__ w, int64_t N, int64_t K, int BN,
+                                    uint8_t* __restrict__ out) {
+  const int64_t kblocks = K / 64;
+  const int64_t tiles_n = (N + BN - 1) / BN;
+  const int64_t chunks = tiles_n * kblocks * BN * 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < chunks;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tile = i / (BN * 8);
+    const int r = (int)((i / 8) % BN), c = (int)(i % 8);
+    const int64_t tn = tile / kblocks, kb = tile % kblocks;
+    const int64_t n = tn * BN + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n < N) v = *reinterpret_cast<const uint4*>(w + n * K + kb * 64 + c * 8);
+    *reinterpret_cast<uint4*>(out + tile * (BN * gemm::KBYTES) + r * gemm::KBYTES + ((c ^ (r & 7)) * 16)) = v;
+  }
+}
+
+
 // out[n][k] = in[k * ld_in + col_idx[n]] for k < K: packs selected columns of a
 // row-major (in, out) weight into a K-major [n, K] operand (32x32 smem tiles).
 __global__ void pack_cols_kernel(const uint16_t* __restrict__ in, int64_t ld_in, int K,
@@ -207,17 +227,25 @@ int upload_idx(const std::vector<int>& v, int** d) {
   return MB_OK;
 }
 
+// Selected columns of a reference (in, out) weight -> K-major [N, K] -> the
+// tiled, pre-swizzled layout every decoder GEMM streams (256-row tiles).
 int pack(const uint16_t* in, int64_t ld_in, int K, const std::vector<int>& cols, uint16_t** out) {
   int* idx = nullptr;
   int rc = upload_idx(cols, &idx);
   if (rc) return rc;
   const int N = (int)cols.size();
-  MB_CUDA(cudaMalloc(out, (size_t)N * K * 2));
+  MB_REQUIRE(K % 64 == 0, "decoder: GEMM inner dimension %d is not a multiple of 64", K);
+  uint16_t* kmajor = nullptr;
+  MB_CUDA(cudaMalloc(&kmajor, (size_t)N * K * 2));
   dim3 g((N + 31) / 32, (K + 31) / 32);
-  pack_cols_kernel<<<g, 256>>>(in, ld_in, K, idx, N, *out);
+  pack_cols_kernel<<<g, 256>>>(in, ld_in, K, idx, N, kmajor);
+  MB_CUDA(cudaGetLastError());
+  MB_CUDA(cudaMalloc(out, tiled_weight_bytes(N, K, 256)));
+  tile_weights_kernel<<<1024, 256>>>(kmajor, N, K, 256, reinterpret_cast<uint8_t*>(*out));
   MB_CUDA(cudaGetLastError());
   MB_CUDA(cudaDeviceSynchronize());
   MB_CUDA(cudaFree(idx));
+  MB_CUDA(cudaFree(kmajor));
   return MB_OK;
 }
 
@@ -293,7 +321,7 @@ Plan make_plan(const Layer& L, int B, int S, int max_kv_len) {
 template <class Epi>
 int gemm_call(const uint16_t* A, const uint16_t* Bw, const Epi& e, int64_t M, int64_t N, int64_t K,
               cudaStream_t s) {
-  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s);
+  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, false, true);
 }
 
 // Partial sums of A @ Bw^T into fp32 slots of part ([slot][M][N]): stream-K
@@ -311,12 +339,12 @@ int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, 
     const StreamK pl = streamk_plan((int)((N + 255) / 256), ps->kblocks, mb::num_sms());
     ps->per = pl.per;
     ps->slots = 0;
-    if (M <= 64) return launch_gemm_decode<256, 5>(A, Bw, e, M, N, K, s);
-    return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, true);
+    if (M <= 64) return launch_gemm_decode<256, 5>(A, Bw, e, M, N, K, s, true);
+    return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, 1, s, true, true);
   }
   ps->per = 0;
   ps->slots = ks;
-  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s);
+  return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s, false, true);
 }
 
 unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }

@@ -134,6 +134,11 @@ struct GemmProducer {
   // that only reaches accumulator rows >= M, which no epilogue stores.
   uint32_t a_rows = BM;
   __device__ uint32_t stage_tx_bytes() const { return PARTS * (a_rows + BN) * KBYTES; }
+  // Optional pre-tiled B (bf16, K-major, see tile_weights in gemm_launch.cuh):
+  // tile (tn, kb) is BN*128 contiguous bytes already in the 128-byte-swizzled
+  // shared-memory image, fetched with one bulk copy instead of a TMA box.
+  const uint8_t* b_tiled = nullptr;
+  int b_kblocks = 0;
   static constexpr int KE = KBYTES / elem_bytes(MODE);  // K elements per stage
   static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;
   static constexpr uint32_t BYTES = PARTS * (BM + BN) * KBYTES;
@@ -156,7 +161,11 @@ struct GemmProducer {
     uint8_t* sB = st + BM * KBYTES;
     mbd::tma_load_2d(sA, &a, bar, kb * KE, tm * BM);
     if constexpr (!B_MN) {
-      mbd::tma_load_2d(sB, &b, bar, kb * KE, tn * BN);
+      if (b_tiled)
+        mbd::bulk_load(sB, b_tiled + ((size_t)tn * b_kblocks + kb) * (BN * KBYTES), BN * KBYTES,
+                       bar);
+      else
+        mbd::tma_load_2d(sB, &b, bar, kb * KE, tn * BN);
     } else {
 #pragma unroll
       for (int j = 0; j < BN / KE; ++j)
@@ -214,6 +223,8 @@ struct DecodeProducer {
   static constexpr int RESIDENT_BYTES = 0;
   static_assert((AROWS * KBYTES) % 1024 == 0, "B box must stay swizzle-atom aligned");
   uint32_t a_rows;  // <= AROWS, multiple of 16
+  const uint8_t* b_tiled = nullptr;  // pre-tiled B (as GemmProducer::b_tiled)
+  int b_kblocks = 0;
   __device__ uint32_t stage_tx_bytes() const { return (a_rows + BN) * KBYTES; }
   __device__ uint32_t resident_tx_bytes() const { return 0; }
   __device__ void prefetch() const {
@@ -223,7 +234,11 @@ struct DecodeProducer {
   __device__ void load_resident(uint8_t*, uint64_t*) const {}
   __device__ void load(uint8_t* st, uint64_t* bar, int tm, int tn, int kb) const {
     mbd::tma_load_2d(st, &a, bar, kb * KE, tm * BM);
-    mbd::tma_load_2d(st + AROWS * KBYTES, &b, bar, kb * KE, tn * BN);
+    if (b_tiled)
+      mbd::bulk_load(st + AROWS * KBYTES, b_tiled + ((size_t)tn * b_kblocks + kb) * (BN * KBYTES),
+                     BN * KBYTES, bar);
+    else
+      mbd::tma_load_2d(st + AROWS * KBYTES, &b, bar, kb * KE, tn * BN);
   }
   __device__ void issue(uint32_t d, uint32_t st, uint32_t, int, bool first) const {
     constexpr uint32_t idesc = mbd::make_idesc(1u, BM, BN, 0, 0);

@@ -22,7 +22,7 @@ inline StreamK streamk_plan(int tiles, int kblocks, int sms) {
 
 template <Mode MODE, int BN, int STAGES, bool B_MN, class Epi>
 inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, int64_t N, int64_t K,
-                int ksplit, cudaStream_t stream, bool streamk = false) {
+                int ksplit, cudaStream_t stream, bool streamk = false, bool b_tiled = false) {
   using P = GemmProducer<MODE, BN, B_MN>;
   using S = Smem<P, BN, STAGES>;
   const int esz = elem_bytes(MODE);
@@ -38,7 +38,12 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
   int rc = mb::make_tmap_2d(&p.a, A, dt, esz, K, M, K * esz, P::KE, p.a_rows,
                             CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (!B_MN)
+  if (b_tiled) {
+    MB_REQUIRE(MODE == Mode::BF16 && !B_MN && K % P::KE == 0,
+               "gemm: tiled B needs bf16, K-major and K %% 64 == 0");
+    p.b_tiled = static_cast<const uint8_t*>(B);
+    p.b_kblocks = (int)(K / P::KE);
+  } else if (!B_MN)
     rc = mb::make_tmap_2d(&p.b, B, dt, esz, K, N, K * esz, P::KE, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   else
     rc = mb::make_tmap_2d(&p.b, B, dt, esz, N, K, N * esz, P::KE, P::KE,
@@ -73,10 +78,20 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
 }
 
 
+// Weight tiling: a K-major bf16 [N, K] matrix (K % 64 == 0) becomes
+// ceil(N/BN) x K/64 tiles, tile (tn, kb) at ((tn * K/64) + kb) * BN * 128 bytes,
+// each holding rows tn*BN.. and k kb*64.. exactly as the 128-byte-swizzled TMA
+// box lands in shared memory: 16-byte chunk c of row r at r*128 + ((c ^ (r%8))*16).
+// Rows past N are zero. A GEMM then streams each stage's B with one
+// contiguous bulk copy. (The tiling kernel is decoder.cu's tile_weights_kernel.)
+inline size_t tiled_weight_bytes(int64_t N, int64_t K, int BN) {
+  return (size_t)((N + BN - 1) / BN) * (size_t)(K / 64) * BN * KBYTES;
+}
+
 // Stream-K GEMM for decode sizes (M <= 64): bf16, B K-major [N, K].
 template <int BN, int STAGES, class Epi>
 inline int launch_gemm_decode(const void* A, const void* B, const Epi& epi, int64_t M, int64_t N,
-                              int64_t K, cudaStream_t stream) {
+                              int64_t K, cudaStream_t stream, bool b_tiled = false) {
   using P = DecodeProducer<BN, 64>;
   using S = Smem<P, BN, STAGES>;
   static_assert(S::TOTAL <= 232448, "decode GEMM: shared memory over the sm_100 limit");
@@ -86,9 +101,14 @@ inline int launch_gemm_decode(const void* A, const void* B, const Epi& epi, int6
   p.a_rows = (uint32_t)((M + 15) / 16 * 16);
   int rc = mb::make_tmap_2d(&p.a, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, K * 2, 64,
                             p.a_rows, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc)
+  if (b_tiled) {
+    MB_REQUIRE(K % 64 == 0, "decode GEMM: tiled B needs K %% 64 == 0");
+    p.b_tiled = static_cast<const uint8_t*>(B);
+    p.b_kblocks = (int)(K / 64);
+  } else if (!rc) {
     rc = mb::make_tmap_2d(&p.b, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, K * 2, 64, BN,
                           CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (rc) return rc;
   Sched sc;
   sc.tiles_m = 1;
