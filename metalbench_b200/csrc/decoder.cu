@@ -518,7 +518,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   }
   MB_CUDA(cudaGetLastError());
   if (L.world > 1) {
-    rc = mb::tp_allreduce_bf16(x1, (size_t)T * D, s);
+    rc = mb::tp_allreduce_sum(x1, (size_t)T * D, s);
     if (rc) return rc;
   }
 
@@ -570,7 +570,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   }
   MB_CUDA(cudaGetLastError());
   if (L.world > 1) {
-    rc = mb::tp_allreduce_bf16(y, (size_t)T * D, s);
+    rc = mb::tp_allreduce_sum(y, (size_t)T * D, s);
     if (rc) return rc;
   }
   return MB_OK;

@@ -60,5 +60,6 @@ int tp_init(int rank, int world, const char* nccl_id_path, int timeout_ms);
 void tp_shutdown();
 int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream);
 int tp_world();
+int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 
 }  // namespace mb
