@@ -8,6 +8,7 @@
 // created non-blocking and polled with ncclCommGetAsyncError until ready or
 // the deadline, after which it is aborted and MB_ERR_TIMEOUT is returned.
 #include <stdio.h>
+#include <string.h>
 #include <unistd.h>
 
 #include <chrono>
@@ -155,118 +156,173 @@ int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------------------
-// One-shot all-reduce over NVLink peer memory.
+// All-reduce over NVLink peer memory (one process per GPU, CUDA IPC).
 //
-// Every rank owns, in its own HBM: staging[2][MAXE] bf16 (double buffer),
-// flags[world] u32 (written by the peers) and two private counters. Peers'
-// staging and flags are mapped with CUDA IPC at set-up (handles exchanged with
-// one NCCL all-gather). A call is two kernels on the caller's stream:
-//   publish: copy my partial into my staging slot (epoch % 2); the last CTA to
-//            finish fences (system scope), stores epoch+1 into flags[my rank] of
-//            every peer (release) and bumps my epoch;
-//   gather:  wait (bounded) until every peer's flag in MY flags array reached
-//            the epoch (acquire), then sum all ranks' staging slots over NVLink
-//            into the output.
-// The epoch lives on the device, so a CUDA graph of the step replays
-// correctly. Two slots suffice: a rank can only republish a slot after every
-// peer has published the following epoch, i.e. after every peer finished
-// reading that slot.
+// Every rank owns one region in its HBM, mapped by every peer at set-up
+// (handles exchanged with one NCCL all-gather):
+//   staging[2][MAXE] bf16   my partial, double-buffered by epoch parity
+//   result [2][MAXE] bf16   two-shot: the reduced chunks pushed by their owners
+//   flags  [64] u32         flags[r] = last epoch rank r published (peers write)
+//   flags2 [64] u32         flags2[r] = last epoch rank r pushed its chunk
+// plus private counters (epoch, CTA arrival counts). The epoch lives on the
+// device, so a CUDA graph of a whole decode step replays correctly.
+//
+//   publish  : copy my partial into staging[e%2]; the last CTA fences at system
+//              scope and stores e+1 into flags[my rank] of every peer (release),
+//              then bumps my epoch.
+//   one-shot : wait until every flags[r] >= e+1 (acquire), sum the W staging
+//              slots over NVLink into the output (W-1 remote reads of n).
+//   two-shot : wait likewise; sum only my chunk n/W, push it into result[e%2]
+//              of every rank (remote stores), last CTA signals flags2; then
+//              wait for every flags2[r] and copy my result slot to the output
+//              (2(W-1)/W of n crosses NVLink per rank instead of (W-1) n).
+// Two slots suffice: a rank republishes a slot only after every peer has
+// published the next epoch, i.e. after every peer finished reading the slot.
+// Every wait is bounded (5 s of %globaltimer) and reports through the device
+// status word.
 // ---------------------------------------------------------------------------
 static constexpr size_t kP2PMaxElems = size_t(4) << 20;  // 8 MiB of bf16 per slot
+static constexpr size_t kP2PRegion =
+    4 * kP2PMaxElems * sizeof(uint16_t) + 2 * 64 * sizeof(uint32_t);
+
+struct Region {  // offsets inside one rank's region
+  static __host__ __device__ uint16_t* staging(void* base, uint32_t slot) {
+    return static_cast<uint16_t*>(base) + (size_t)slot * kP2PMaxElems;
+  }
+  static __host__ __device__ uint16_t* result(void* base, uint32_t slot) {
+    return static_cast<uint16_t*>(base) + (size_t)(2 + slot) * kP2PMaxElems;
+  }
+  static __host__ __device__ uint32_t* flags(void* base) {
+    return reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(base) + 4 * kP2PMaxElems);
+  }
+  static __host__ __device__ uint32_t* flags2(void* base) { return flags(base) + 64; }
+};
+
 struct P2P {
   bool ready = false;
   int rank = 0, world = 1;
-  uint16_t* staging = nullptr;  // local [2][MAXE]
-  uint32_t* flags = nullptr;    // local [world]
-  uint32_t* ctr = nullptr;      // local: [0] epoch, [1] CTAs done
-  uint16_t* peer_staging[8] = {};
-  uint32_t* peer_flags[8] = {};
+  void* region = nullptr;     // local
+  uint32_t* ctr = nullptr;    // local: [0] epoch, [1] publish arrivals, [2] push arrivals
+  void* peer[8] = {};         // peer regions (peer[rank] = region)
 };
 static P2P g_p2p;
 
 struct PeerPtrs {
-  const uint16_t* staging[8];
-  uint32_t* flags[8];
+  void* r[8];
 };
 
-__global__ void p2p_publish_kernel(const uint16_t* __restrict__ src, size_t n, uint16_t* staging,
-                                   PeerPtrs peers, uint32_t* ctr, int rank, int world) {
-  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]);
-  uint16_t* dst = staging + (size_t)(e & 1) * kP2PMaxElems;
-  const size_t n8 = n / 8;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8;
-       i += (size_t)gridDim.x * blockDim.x)
-    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
-  for (size_t i = n8 * 8 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x)
-    dst[i] = src[i];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const uint32_t done = atomicAdd(&ctr[1], 1u) + 1;
-    if (done == gridDim.x) {  // last CTA: everything of this rank is written
-      __threadfence_system();
-      for (int r = 0; r < world; ++r)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.flags[r] + rank), "r"(e + 1)
-                     : "memory");
-      ctr[1] = 0;
-      ctr[0] = e + 1;
-    }
-  }
+__device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
-__global__ void p2p_gather_kernel(uint16_t* __restrict__ out, size_t n, PeerPtrs peers,
-                                  const uint32_t* flags, const uint32_t* ctr, int world,
-                                  uint32_t* status) {
-  __shared__ int ok;
-  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(&ctr[0]);  // already bumped
+// Threads 0..world-1 of the CTA wait for flags[r] >= e; then a CTA barrier.
+__device__ __forceinline__ void wait_flags(const uint32_t* flags, uint32_t e, int world,
+                                           uint32_t* status) {
   if (threadIdx.x < (unsigned)world) {
     const uint64_t t0 = mbd::globaltimer_ns();
-    uint32_t v = 0;
     for (uint32_t it = 0;; ++it) {
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + threadIdx.x)
-                   : "memory");
-      if ((int32_t)(v - e) >= 0) break;
+      if ((int32_t)(load_acquire_sys(flags + threadIdx.x) - e) >= 0) break;
       if ((it & 63u) == 0 && mbd::globaltimer_ns() - t0 > 5000000000ull) {
         atomicOr(status, MB_DEV_TIMEOUT_EPI);
         break;
       }
     }
   }
-  if (threadIdx.x == 0) ok = 1;
   __syncthreads();
-  const size_t slot = (size_t)((e - 1) & 1) * kP2PMaxElems;
-  const size_t n8 = n / 8;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8;
-       i += (size_t)gridDim.x * blockDim.x) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int r = 0; r < world; ++r) {
-      const uint4 w = reinterpret_cast<const uint4*>(peers.staging[r] + slot)[i];
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+}
+
+__device__ __forceinline__ void acc8(float (&a)[8], uint4 w) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        acc[2 * m] += __uint_as_float(ws[m] << 16);
-        acc[2 * m + 1] += __uint_as_float(ws[m] & 0xFFFF0000u);
-      }
-    }
-    uint4 o;
-    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * m], acc[2 * m + 1]);
-      op[m] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    reinterpret_cast<uint4*>(out)[i] = o;
+  for (int m = 0; m < 4; ++m) {
+    a[2 * m] += __uint_as_float(ws[m] << 16);
+    a[2 * m + 1] += __uint_as_float(ws[m] & 0xFFFF0000u);
   }
-  for (size_t i = n8 * 8 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+}
+__device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * m], a[2 * m + 1]);
+    op[m] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return o;
+}
+
+// n is a multiple of 8 * world (checked by the host).
+__global__ void p2p_publish_kernel(const uint16_t* __restrict__ src, size_t n, PeerPtrs peers,
+                                   uint32_t* ctr, int rank, int world) {
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]);
+  uint16_t* dst = Region::staging(peers.r[rank], e & 1);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 8;
+       i += (size_t)gridDim.x * blockDim.x)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(&ctr[1], 1u) + 1 == gridDim.x) {  // the last CTA of this rank
+      __threadfence_system();
+      for (int r = 0; r < world; ++r) store_release_sys(Region::flags(peers.r[r]) + rank, e + 1);
+      ctr[1] = 0;
+      ctr[0] = e + 1;
+    }
+  }
+}
+
+__global__ void p2p_oneshot_kernel(uint16_t* __restrict__ out, size_t n, PeerPtrs peers,
+                                   const uint32_t* ctr, int rank, int world, uint32_t* status) {
+  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(&ctr[0]);  // already bumped
+  wait_flags(Region::flags(peers.r[rank]), e, world, status);
+  const uint32_t slot = (e - 1) & 1;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 8;
        i += (size_t)gridDim.x * blockDim.x) {
-    float a = 0.f;
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int r = 0; r < world; ++r)
-      a += __uint_as_float(((uint32_t)peers.staging[r][slot + i]) << 16);
-    __nv_bfloat16 h = __float2bfloat16_rn(a);
-    out[i] = *reinterpret_cast<uint16_t*>(&h);
+      acc8(a, reinterpret_cast<const uint4*>(Region::staging(peers.r[r], slot))[i]);
+    reinterpret_cast<uint4*>(out)[i] = pack8(a);
   }
-  (void)ok;
+}
+
+__global__ void p2p_reduce_push_kernel(size_t n, PeerPtrs peers, uint32_t* ctr, int rank,
+                                       int world, uint32_t* status) {
+  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(&ctr[0]);
+  wait_flags(Region::flags(peers.r[rank]), e, world, status);
+  const uint32_t slot = (e - 1) & 1;
+  const size_t chunk8 = n / 8 / world, c0 = (size_t)rank * chunk8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunk8;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = 0; r < world; ++r)
+      acc8(a, reinterpret_cast<const uint4*>(Region::staging(peers.r[r], slot))[c0 + i]);
+    const uint4 o = pack8(a);
+    for (int r = 0; r < world; ++r)
+      reinterpret_cast<uint4*>(Region::result(peers.r[r], slot))[c0 + i] = o;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(&ctr[2], 1u) + 1 == gridDim.x) {
+      __threadfence_system();
+      for (int r = 0; r < world; ++r) store_release_sys(Region::flags2(peers.r[r]) + rank, e);
+      ctr[2] = 0;
+    }
+  }
+}
+
+__global__ void p2p_collect_kernel(uint16_t* __restrict__ out, size_t n, PeerPtrs peers,
+                                   const uint32_t* ctr, int rank, int world, uint32_t* status) {
+  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(&ctr[0]);
+  wait_flags(Region::flags2(peers.r[rank]), e, world, status);
+  const uint4* res = reinterpret_cast<const uint4*>(Region::result(peers.r[rank], (e - 1) & 1));
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 8;
+       i += (size_t)gridDim.x * blockDim.x)
+    reinterpret_cast<uint4*>(out)[i] = res[i];
 }
 
 #ifdef MB_HAVE_NCCL
@@ -278,43 +334,35 @@ static int p2p_setup(int rank, int world) {
   P2P& p = g_p2p;
   p.rank = rank;
   p.world = world;
-  MB_CUDA(cudaMalloc(&p.staging, 2 * kP2PMaxElems * sizeof(uint16_t)));
-  MB_CUDA(cudaMalloc(&p.flags, 64 * sizeof(uint32_t)));
-  MB_CUDA(cudaMalloc(&p.ctr, 2 * sizeof(uint32_t)));
-  MB_CUDA(cudaMemset(p.flags, 0, 64 * sizeof(uint32_t)));
-  MB_CUDA(cudaMemset(p.ctr, 0, 2 * sizeof(uint32_t)));
-  cudaIpcMemHandle_t mine[2];
-  MB_CUDA(cudaIpcGetMemHandle(&mine[0], p.staging));
-  MB_CUDA(cudaIpcGetMemHandle(&mine[1], p.flags));
+  MB_CUDA(cudaMalloc(&p.region, kP2PRegion));
+  MB_CUDA(cudaMemset(p.region, 0, kP2PRegion));
+  MB_CUDA(cudaMalloc(&p.ctr, 4 * sizeof(uint32_t)));
+  MB_CUDA(cudaMemset(p.ctr, 0, 4 * sizeof(uint32_t)));
+  cudaIpcMemHandle_t mine;
+  MB_CUDA(cudaIpcGetMemHandle(&mine, p.region));
   void* dmine = nullptr;
   void* dall = nullptr;
   MB_CUDA(cudaMalloc(&dmine, sizeof(mine)));
   MB_CUDA(cudaMalloc(&dall, sizeof(mine) * world));
-  MB_CUDA(cudaMemcpy(dmine, mine, sizeof(mine), cudaMemcpyHostToDevice));
+  MB_CUDA(cudaMemcpy(dmine, &mine, sizeof(mine), cudaMemcpyHostToDevice));
   ncclResult_t r = ncclAllGather(dmine, dall, sizeof(mine), ncclUint8, g_comm, 0);
   if (r == ncclInProgress) {
-    int rc = wait_ready(60000, "handle all-gather");
+    int rc = wait_ready(60000, "IPC handle all-gather");
     if (rc) return rc;
   } else if (r != ncclSuccess) {
     return nccl_fail(r, "ncclAllGather(ipc handles)");
   }
   MB_CUDA(cudaDeviceSynchronize());
-  std::vector<cudaIpcMemHandle_t> all(2 * world);
+  std::vector<cudaIpcMemHandle_t> all(world);
   MB_CUDA(cudaMemcpy(all.data(), dall, sizeof(mine) * world, cudaMemcpyDeviceToHost));
   cudaFree(dmine);
   cudaFree(dall);
   for (int q = 0; q < world; ++q) {
     if (q == rank) {
-      p.peer_staging[q] = p.staging;
-      p.peer_flags[q] = p.flags;
+      p.peer[q] = p.region;
       continue;
     }
-    void* a = nullptr;
-    void* b = nullptr;
-    MB_CUDA(cudaIpcOpenMemHandle(&a, all[2 * q], cudaIpcMemLazyEnablePeerAccess));
-    MB_CUDA(cudaIpcOpenMemHandle(&b, all[2 * q + 1], cudaIpcMemLazyEnablePeerAccess));
-    p.peer_staging[q] = static_cast<uint16_t*>(a);
-    p.peer_flags[q] = static_cast<uint32_t*>(b);
+    MB_CUDA(cudaIpcOpenMemHandle(&p.peer[q], all[q], cudaIpcMemLazyEnablePeerAccess));
   }
   p.ready = true;
   return MB_OK;
@@ -325,38 +373,42 @@ static void p2p_teardown() {
   P2P& p = g_p2p;
   if (!p.ready) return;
   for (int q = 0; q < p.world; ++q)
-    if (q != p.rank) {
-      if (p.peer_staging[q]) cudaIpcCloseMemHandle(p.peer_staging[q]);
-      if (p.peer_flags[q]) cudaIpcCloseMemHandle(p.peer_flags[q]);
-    }
-  cudaFree(p.staging);
-  cudaFree(p.flags);
+    if (q != p.rank && p.peer[q]) cudaIpcCloseMemHandle(p.peer[q]);
+  cudaFree(p.region);
   cudaFree(p.ctr);
   p = P2P();
 }
 
-// All-reduce used by the decoder: the peer kernels for messages that fit a
-// staging slot (decode), NCCL otherwise or when MB_TP_NCCL=1.
+// All-reduce used by the decoder: the peer kernels (two-shot by default,
+// MB_TP_P2P=1shot for one-shot) for messages that fit a staging slot, NCCL
+// otherwise or when MB_TP_NCCL is set.
 int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream) {
   static const bool force_nccl = getenv("MB_TP_NCCL") != nullptr;
-  if (!g_p2p.ready || force_nccl || count > kP2PMaxElems) return tp_allreduce_bf16(buf, count, stream);
+  static const bool oneshot = getenv("MB_TP_P2P") && !strcmp(getenv("MB_TP_P2P"), "1shot");
+  if (!g_p2p.ready || force_nccl || count > kP2PMaxElems || count % (8 * g_p2p.world) != 0 ||
+      reinterpret_cast<uintptr_t>(buf) % 16 != 0)
+    return tp_allreduce_bf16(buf, count, stream);
   PeerPtrs pp;
-  for (int q = 0; q < 8; ++q) {
-    pp.staging[q] = g_p2p.peer_staging[q];
-    pp.flags[q] = g_p2p.peer_flags[q];
-  }
-  const int sms = num_sms();
-  const size_t n8 = (count + 7) / 8;
-  int blocks = (int)((n8 + 255) / 256);
-  if (blocks > 2 * sms) blocks = 2 * sms;
-  if (blocks < 1) blocks = 1;
-  p2p_publish_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(buf), count,
-                                                  g_p2p.staging, pp, g_p2p.ctr, g_p2p.rank,
-                                                  g_p2p.world);
+  for (int q = 0; q < 8; ++q) pp.r[q] = g_p2p.peer[q];
+  const int W = g_p2p.world, R = g_p2p.rank;
+  auto grid = [](size_t vec) {
+    int b = (int)((vec + 255) / 256);
+    const int cap = 2 * num_sms();
+    return b < 1 ? 1 : (b > cap ? cap : b);
+  };
+  uint16_t* x = static_cast<uint16_t*>(buf);
+  p2p_publish_kernel<<<grid(count / 8), 256, 0, stream>>>(x, count, pp, g_p2p.ctr, R, W);
   MB_CUDA(cudaGetLastError());
-  p2p_gather_kernel<<<blocks, 256, 0, stream>>>(static_cast<uint16_t*>(buf), count, pp,
-                                                 g_p2p.flags, g_p2p.ctr, g_p2p.world,
-                                                 device_status_ptr());
+  if (oneshot) {
+    p2p_oneshot_kernel<<<grid(count / 8), 256, 0, stream>>>(x, count, pp, g_p2p.ctr, R, W,
+                                                            device_status_ptr());
+  } else {
+    p2p_reduce_push_kernel<<<grid(count / 8 / W), 256, 0, stream>>>(count, pp, g_p2p.ctr, R, W,
+                                                                     device_status_ptr());
+    MB_CUDA(cudaGetLastError());
+    p2p_collect_kernel<<<grid(count / 8), 256, 0, stream>>>(x, count, pp, g_p2p.ctr, R, W,
+                                                            device_status_ptr());
+  }
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
