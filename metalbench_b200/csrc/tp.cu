@@ -115,7 +115,7 @@ int tp_init(int rank, int world, const char* nccl_id_path, int timeout_ms) {
   int rc = wait_ready(timeout_ms, "NCCL communicator set-up");
   if (rc) return rc;
   g_world = world;
-  if (getenv("MB_TP_NO_P2P") == nullptr) {
+  if (getenv("MB_TP_P2P") != nullptr) {  // peer all-reduce requested: map the peers
     rc = p2p_setup(rank, world);
     if (rc) return rc;
   }
@@ -379,12 +379,15 @@ static void p2p_teardown() {
   p = P2P();
 }
 
-// All-reduce used by the decoder: the peer kernels (two-shot by default,
-// MB_TP_P2P=1shot for one-shot) for messages that fit a staging slot, NCCL
-// otherwise or when MB_TP_NCCL is set.
+// All-reduce used by the decoder. NCCL by default: on 8 B200s with NVLS it
+// measured faster than both peer variants at the decode message size (1 MiB:
+// stack decode 30958 tok/s with NCCL, 28442 one-shot, 24894 two-shot).
+// MB_TP_P2P=1shot|2shot selects the peer kernels for messages that fit a slot.
 int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream) {
-  static const bool force_nccl = getenv("MB_TP_NCCL") != nullptr;
-  static const bool oneshot = getenv("MB_TP_P2P") && !strcmp(getenv("MB_TP_P2P"), "1shot");
+  static const char* mode = getenv("MB_TP_P2P");
+  static const bool use_p2p = mode && (!strcmp(mode, "1shot") || !strcmp(mode, "2shot"));
+  static const bool force_nccl = !use_p2p || getenv("MB_TP_NCCL") != nullptr;
+  static const bool oneshot = use_p2p && !strcmp(mode, "1shot");
   if (!g_p2p.ready || force_nccl || count > kP2PMaxElems || count % (8 * g_p2p.world) != 0 ||
       reinterpret_cast<uintptr_t>(buf) % 16 != 0)
     return tp_allreduce_bf16(buf, count, stream);
