@@ -223,9 +223,6 @@ struct Layer {
   // start at zero and the finishing CTA of every tile puts them back to zero,
   // so one layer must not run on two streams at once.
   int* counters;
-  // fp32 accumulator of the decode GEMMs ([64][max N]); zero between launches
-  // (each finishing CTA re-zeroes its tile).
-  float* acc;
 };
 
 int upload_idx(const std::vector<int>& v, int** d) {
@@ -357,14 +354,13 @@ int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, 
 // Decode GEMM (M <= 64) as ONE kernel: stream-K over the pre-tiled weight with
 // the final epilogue applied by the last CTA of every tile (dec::EpiStreamK).
 template <class Fin>
-int gemm_fused_decode(const uint16_t* A, const uint16_t* Bw, float* acc, int* counters,
+int gemm_fused_decode(const uint16_t* A, const uint16_t* Bw, float* part, int* counters,
                       int64_t M, int64_t N, int64_t K, const Fin& fin, cudaStream_t s) {
   MB_REQUIRE((N + 255) / 256 <= 512, "decode GEMM: more than 512 column tiles");
-  MB_REQUIRE(M <= 64 && N % 4 == 0, "decode GEMM: M <= 64 and N %% 4 == 0 required");
   dec::EpiStreamK<Fin> e;
   e.M = (int)M;
   e.N = (int)N;
-  e.acc = acc;
+  e.ws = part;
   e.counters = counters;
   e.kblocks = (int)((K + 63) / 64);
   e.per = streamk_plan((int)((N + 255) / 256), e.kblocks, mb::num_sms()).per;
@@ -419,12 +415,8 @@ extern "C" int mb_decoder_layer_create(const mb_decoder_config* cfg, const uint1
   if (!rc) rc = pack(W_gu, 2 * FF, D, gu, &L->wgu);
   if (!rc) rc = pack(W_down + (int64_t)tp_rank * L->FF * D, D, L->FF, ident, &L->wdown);
   if (!rc) {
-    const size_t maxN = std::max<size_t>(std::max<size_t>(L->Dq + 2 * L->Dkv, D), 2 * L->FF);
-    const size_t acc_bytes = 64 * maxN * sizeof(float);
     if (cudaMalloc(&L->counters, 4 * 512 * sizeof(int)) != cudaSuccess ||
-        cudaMemset(L->counters, 0, 4 * 512 * sizeof(int)) != cudaSuccess ||
-        cudaMalloc(&L->acc, acc_bytes) != cudaSuccess ||
-        cudaMemset(L->acc, 0, acc_bytes) != cudaSuccess) {
+        cudaMemset(L->counters, 0, 4 * 512 * sizeof(int)) != cudaSuccess) {
       mb::set_error("decoder create: cannot allocate tile counters");
       rc = MB_ERR_CUDA;
     }
@@ -445,7 +437,6 @@ extern "C" void mb_decoder_layer_destroy(void* layer) {
   cudaFree(L->wgu);
   cudaFree(L->wdown);
   cudaFree(L->counters);
-  cudaFree(L->acc);
   delete L;
 }
 
@@ -503,7 +494,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   qp.kv = dec::KvCache{k_cache, v_cache, block_table, max_pages, 64};
   const bool fused = T <= 64;  // decode: one kernel per GEMM (stream-K + fix-up)
   if (fused) {
-    rc = gemm_fused_decode(x, L.wqkv, L.acc, L.counters, T, Nqkv, D, dec::FinQkv{qp}, s);
+    rc = gemm_fused_decode(x, L.wqkv, part, L.counters, T, Nqkv, D, dec::FinQkv{qp}, s);
     if (rc) return rc;
   } else if (p.ks_qkv > 1 || use_streamk(T, Nqkv)) {
     PartSum ps;
@@ -541,7 +532,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   eo.residual = L.rank == 0 ? x : nullptr;
   eo.ld_res = D;
   if (fused) {
-    rc = gemm_fused_decode(attn, L.wo, L.acc, L.counters + 512, T, D, L.Dq, dec::FinStore{eo}, s);
+    rc = gemm_fused_decode(attn, L.wo, part, L.counters + 512, T, D, L.Dq, dec::FinStore{eo}, s);
     if (rc) return rc;
   } else if (p.ks_o > 1 || use_streamk(T, D)) {
     PartSum ps;
@@ -578,7 +569,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   sp.rstd = rstd2;
   sp.act = act;
   if (fused) {
-    rc = gemm_fused_decode(x1, L.wgu, L.acc, L.counters + 1024, T, 2 * L.FF, D, dec::FinSwiglu{sp},
+    rc = gemm_fused_decode(x1, L.wgu, part, L.counters + 1024, T, 2 * L.FF, D, dec::FinSwiglu{sp},
                            s);
     if (rc) return rc;
   } else if (p.ks_gu > 1 || use_streamk(T, 2 * L.FF)) {
@@ -606,7 +597,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   ed.residual = L.rank == 0 ? x1 : nullptr;
   ed.ld_res = D;
   if (fused) {
-    rc = gemm_fused_decode(act, L.wdown, L.acc, L.counters + 1536, T, D, L.FF, dec::FinStore{ed}, s);
+    rc = gemm_fused_decode(act, L.wdown, part, L.counters + 1536, T, D, L.FF, dec::FinStore{ed}, s);
     if (rc) return rc;
   } else if (p.ks_down > 1 || use_streamk(T, D)) {
     PartSum ps;

@@ -152,41 +152,34 @@ struct EpiPartial {
 namespace dec {
 
 // ---------------------------------------------------------------------------
-// Stream-K with in-kernel fix-up (decode GEMMs, M <= 64): every CTA adds the
-// fp32 partial of its (tile, segment) into one accumulator with vector
-// reductions in L2 (red.global.add.v4.f32), fences, and bumps the tile's
-// arrival counter. The CTA that arrives last — it never waits for anyone —
-// reads the tile's sums, writes zeros back (so the accumulator is clean for
-// the next launch, CUDA graphs included) and applies the final epilogue; it
-// also resets the counter. No separate reduce kernel. The order of the fp32
-// additions depends on arrival, so the last bits of a sum can differ from run
-// to run (well inside the bf16 output precision).
-// Tiles are the 256-wide column blocks of a single tile row.
+// Stream-K with in-kernel fix-up (decode GEMMs): every CTA writes the fp32
+// partial of its (tile, segment) into slot `seg` of ws, fences, and bumps the
+// tile's arrival counter. The CTA that arrives last — it never waits for
+// anyone — sums the tile's segments and applies the final epilogue, then
+// resets the counter for the next launch. No separate reduce kernel.
+// Tiles are the 256-wide column blocks of a single tile row (M <= 128).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
-
-// Read 8 accumulated values (from L2: written by other SMs) and zero them.
-__device__ __forceinline__ void take8(float* p, float (&v)[8]) {
-  float4* q = reinterpret_cast<float4*>(p);
-  const float4 a = __ldcg(q), b = __ldcg(q + 1);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  __stcg(q, make_float4(0.f, 0.f, 0.f, 0.f));
-  __stcg(q + 1, make_float4(0.f, 0.f, 0.f, 0.f));
+__device__ __forceinline__ void slot_sum8(const float* ws, int nseg, int64_t stride, int N, int row,
+                                          int col, float (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  for (int s = 0; s < nseg; ++s) {
+    const float4* p = reinterpret_cast<const float4*>(ws + s * stride + (int64_t)row * N + col);
+    const float4 a = __ldcg(p), b = __ldcg(p + 1);  // L2: written by other SMs
+    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+  }
 }
 
 struct FinStore {  // out = scale * acc + residual
   gemm::EpiStore e;
-  __device__ void finish(float* acc, int M, int N, int n0, int tid, int nt) const {
+  __device__ void finish(const float* ws, int nseg, int64_t stride, int M, int N, int n0, int tid,
+                         int nt) const {
     for (int i = tid; i < M * 32; i += nt) {
       const int row = i / 32, col = n0 + (i % 32) * 8;
       if (col >= N) continue;
       float v[8];
-      take8(acc + (int64_t)row * N + col, v);
+      slot_sum8(ws, nseg, stride, N, row, col, v);
       const float sc = e.row_scale ? e.row_scale[row] * e.alpha : e.alpha;
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] *= sc;
@@ -206,12 +199,13 @@ struct FinStore {  // out = scale * acc + residual
 
 struct FinQkv {  // RMSNorm scale, RoPE, q store, paged KV write
   QkvParams q;
-  __device__ void finish(float* acc, int M, int N, int n0, int tid, int nt) const {
+  __device__ void finish(const float* ws, int nseg, int64_t stride, int M, int N, int n0, int tid,
+                         int nt) const {
     for (int i = tid; i < M * 32; i += nt) {
       const int row = i / 32, col = n0 + (i % 32) * 8;
       if (col >= N) continue;
       float v[8];
-      take8(acc + (int64_t)row * N + col, v);
+      slot_sum8(ws, nseg, stride, N, row, col, v);
       q.apply<8>(row, col, v);
     }
   }
@@ -219,12 +213,13 @@ struct FinQkv {  // RMSNorm scale, RoPE, q store, paged KV write
 
 struct FinSwiglu {  // tile = 128 gate + 128 up columns -> 128 features
   SwigluParams p;
-  __device__ void finish(float* acc, int M, int N, int n0, int tid, int nt) const {
+  __device__ void finish(const float* ws, int nseg, int64_t stride, int M, int N, int n0, int tid,
+                         int nt) const {
     for (int i = tid; i < M * 16; i += nt) {
       const int row = i / 16, j = (i % 16) * 8;
       float g[8], u[8];
-      take8(acc + (int64_t)row * N + n0 + j, g);
-      take8(acc + (int64_t)row * N + n0 + 128 + j, u);
+      slot_sum8(ws, nseg, stride, N, row, n0 + j, g);
+      slot_sum8(ws, nseg, stride, N, row, n0 + 128 + j, u);
       p.apply<8>(row, (n0 / 256) * 128 + j, g, u);
     }
   }
@@ -233,8 +228,8 @@ struct FinSwiglu {  // tile = 128 gate + 128 up columns -> 128 features
 template <class Fin>
 struct EpiStreamK {
   int M, N;
-  float* acc;      // [M][N] fp32, all zero between launches
-  int* counters;   // [tiles], zero between launches
+  float* ws;       // [slots][M][N] fp32
+  int* counters;   // [tiles], zero before the first launch, left zero after
   int kblocks, per;
   Fin fin;
   __device__ void operator()(const gemm::EpiCtx& c) const {
@@ -243,16 +238,14 @@ struct EpiStreamK {
       float v[32];
       gemm::tmem_ld32(c.taddr + c0, v);
       if (!c.row_ok || c.n0 + c0 >= N) continue;
-      float* p = acc + (int64_t)c.row * N + c.n0 + c0;
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) red_add4(p + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+      gemm::store_row32(ws + (int64_t)c.ks * M * N, N, 1, c.row, c.n0 + c0, N, v);
     }
     const int t = c.n0 / 256;
     const int first = (int)(((long long)t * kblocks) / per);
     const int last = (int)(((long long)(t + 1) * kblocks - 1) / per);
     const int nseg = last - first + 1;
     __shared__ int s_last;
-    __threadfence();  // my additions are visible before the arrival is counted
+    __threadfence();  // my partial is visible before the arrival is counted
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
     if (threadIdx.x == 128) {
       const int prev = atomicAdd(&counters[t], 1);
@@ -262,7 +255,7 @@ struct EpiStreamK {
     asm volatile("bar.sync 1, 128;" ::: "memory");
     if (!s_last) return;
     __threadfence();
-    fin.finish(acc, M, N, c.n0, (int)threadIdx.x - 128, 128);
+    fin.finish(ws, nseg, (int64_t)M * N, M, N, c.n0, (int)threadIdx.x - 128, 128);
   }
 };
 
