@@ -218,11 +218,7 @@ struct Layer {
   mb_decoder_config cfg;
   int rank, world;
   int Hq, Hkv, Dq, Dkv, FF;  // per-rank
-  uint16_t *wqkv, *wo, *wgu, *wdown;  // packed, tiled (see pack())
-  // Stream-K tile arrival counters of the four decode GEMMs (512 each). They
-  // start at zero and the finishing CTA of every tile puts them back to zero,
-  // so one layer must not run on two streams at once.
-  int* counters;
+  uint16_t *wqkv, *wo, *wgu, *wdown;  // packed K-major
 };
 
 int upload_idx(const std::vector<int>& v, int** d) {
@@ -351,23 +347,6 @@ int gemm_partial(const uint16_t* A, const uint16_t* Bw, float* part, int64_t M, 
   return launch_gemm<Mode::BF16, 256, 4, false>(A, Bw, e, M, N, K, ks, s, false, true);
 }
 
-// Decode GEMM (M <= 64) as ONE kernel: stream-K over the pre-tiled weight with
-// the final epilogue applied by the last CTA of every tile (dec::EpiStreamK).
-template <class Fin>
-int gemm_fused_decode(const uint16_t* A, const uint16_t* Bw, float* part, int* counters,
-                      int64_t M, int64_t N, int64_t K, const Fin& fin, cudaStream_t s) {
-  MB_REQUIRE((N + 255) / 256 <= 512, "decode GEMM: more than 512 column tiles");
-  dec::EpiStreamK<Fin> e;
-  e.M = (int)M;
-  e.N = (int)N;
-  e.ws = part;
-  e.counters = counters;
-  e.kblocks = (int)((K + 63) / 64);
-  e.per = streamk_plan((int)((N + 255) / 256), e.kblocks, mb::num_sms()).per;
-  e.fin = fin;
-  return launch_gemm_decode<256, 5>(A, Bw, e, M, N, K, s, true);
-}
-
 unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
 
 
@@ -414,13 +393,6 @@ extern "C" int mb_decoder_layer_create(const mb_decoder_config* cfg, const uint1
   }
   if (!rc) rc = pack(W_gu, 2 * FF, D, gu, &L->wgu);
   if (!rc) rc = pack(W_down + (int64_t)tp_rank * L->FF * D, D, L->FF, ident, &L->wdown);
-  if (!rc) {
-    if (cudaMalloc(&L->counters, 4 * 512 * sizeof(int)) != cudaSuccess ||
-        cudaMemset(L->counters, 0, 4 * 512 * sizeof(int)) != cudaSuccess) {
-      mb::set_error("decoder create: cannot allocate tile counters");
-      rc = MB_ERR_CUDA;
-    }
-  }
   if (rc) {
     delete L;
     return rc;
@@ -436,7 +408,6 @@ extern "C" void mb_decoder_layer_destroy(void* layer) {
   cudaFree(L->wo);
   cudaFree(L->wgu);
   cudaFree(L->wdown);
-  cudaFree(L->counters);
   delete L;
 }
 
@@ -492,11 +463,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   qp.start_pos = start_pos;
   qp.q_out = q;
   qp.kv = dec::KvCache{k_cache, v_cache, block_table, max_pages, 64};
-  const bool fused = T <= 64;  // decode: one kernel per GEMM (stream-K + fix-up)
-  if (fused) {
-    rc = gemm_fused_decode(x, L.wqkv, part, L.counters, T, Nqkv, D, dec::FinQkv{qp}, s);
-    if (rc) return rc;
-  } else if (p.ks_qkv > 1 || use_streamk(T, Nqkv)) {
+  if (p.ks_qkv > 1 || use_streamk(T, Nqkv)) {
     PartSum ps;
     rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s, &ps);
     if (rc) return rc;
@@ -531,10 +498,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   eo.alpha = 1.f;
   eo.residual = L.rank == 0 ? x : nullptr;
   eo.ld_res = D;
-  if (fused) {
-    rc = gemm_fused_decode(attn, L.wo, part, L.counters + 512, T, D, L.Dq, dec::FinStore{eo}, s);
-    if (rc) return rc;
-  } else if (p.ks_o > 1 || use_streamk(T, D)) {
+  if (p.ks_o > 1 || use_streamk(T, D)) {
     PartSum ps;
     rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s, &ps);
     if (rc) return rc;
@@ -568,11 +532,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   sp.FF = L.FF;
   sp.rstd = rstd2;
   sp.act = act;
-  if (fused) {
-    rc = gemm_fused_decode(x1, L.wgu, part, L.counters + 1024, T, 2 * L.FF, D, dec::FinSwiglu{sp},
-                           s);
-    if (rc) return rc;
-  } else if (p.ks_gu > 1 || use_streamk(T, 2 * L.FF)) {
+  if (p.ks_gu > 1 || use_streamk(T, 2 * L.FF)) {
     PartSum ps;
     rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s, &ps);
     if (rc) return rc;
@@ -596,10 +556,7 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   ed.alpha = 1.f;
   ed.residual = L.rank == 0 ? x1 : nullptr;
   ed.ld_res = D;
-  if (fused) {
-    rc = gemm_fused_decode(act, L.wdown, part, L.counters + 1536, T, D, L.FF, dec::FinStore{ed}, s);
-    if (rc) return rc;
-  } else if (p.ks_down > 1 || use_streamk(T, D)) {
+  if (p.ks_down > 1 || use_streamk(T, D)) {
     PartSum ps;
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s, &ps);
     if (rc) return rc;

@@ -148,115 +148,3 @@ struct EpiPartial {
 };
 
 }  // namespace dec
-
-namespace dec {
-
-// ---------------------------------------------------------------------------
-// Stream-K with in-kernel fix-up (decode GEMMs): every CTA writes the fp32
-// partial of its (tile, segment) into slot `seg` of ws, fences, and bumps the
-// tile's arrival counter. The CTA that arrives last — it never waits for
-// anyone — sums the tile's segments and applies the final epilogue, then
-// resets the counter for the next launch. No separate reduce kernel.
-// Tiles are the 256-wide column blocks of a single tile row (M <= 128).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void slot_sum8(const float* ws, int nseg, int64_t stride, int N, int row,
-                                          int col, float (&v)[8]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = 0.f;
-  for (int s = 0; s < nseg; ++s) {
-    const float4* p = reinterpret_cast<const float4*>(ws + s * stride + (int64_t)row * N + col);
-    const float4 a = __ldcg(p), b = __ldcg(p + 1);  // L2: written by other SMs
-    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-    v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
-  }
-}
-
-struct FinStore {  // out = scale * acc + residual
-  gemm::EpiStore e;
-  __device__ void finish(const float* ws, int nseg, int64_t stride, int M, int N, int n0, int tid,
-                         int nt) const {
-    for (int i = tid; i < M * 32; i += nt) {
-      const int row = i / 32, col = n0 + (i % 32) * 8;
-      if (col >= N) continue;
-      float v[8];
-      slot_sum8(ws, nseg, stride, N, row, col, v);
-      const float sc = e.row_scale ? e.row_scale[row] * e.alpha : e.alpha;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= sc;
-      if (e.residual) {
-        const uint4 w = *reinterpret_cast<const uint4*>(e.residual + (int64_t)row * e.ld_res + col);
-        const uint32_t ws4[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          v[2 * m] += __uint_as_float(ws4[m] << 16);
-          v[2 * m + 1] += __uint_as_float(ws4[m] & 0xFFFF0000u);
-        }
-      }
-      gemm::store_rowW<8>(e.out, e.ldo, e.out_f32, row, col, e.N, v);
-    }
-  }
-};
-
-struct FinQkv {  // RMSNorm scale, RoPE, q store, paged KV write
-  QkvParams q;
-  __device__ void finish(const float* ws, int nseg, int64_t stride, int M, int N, int n0, int tid,
-                         int nt) const {
-    for (int i = tid; i < M * 32; i += nt) {
-      const int row = i / 32, col = n0 + (i % 32) * 8;
-      if (col >= N) continue;
-      float v[8];
-      slot_sum8(ws, nseg, stride, N, row, col, v);
-      q.apply<8>(row, col, v);
-    }
-  }
-};
-
-struct FinSwiglu {  // tile = 128 gate + 128 up columns -> 128 features
-  SwigluParams p;
-  __device__ void finish(const float* ws, int nseg, int64_t stride, int M, int N, int n0, int tid,
-                         int nt) const {
-    for (int i = tid; i < M * 16; i += nt) {
-      const int row = i / 16, j = (i % 16) * 8;
-      float g[8], u[8];
-      slot_sum8(ws, nseg, stride, N, row, n0 + j, g);
-      slot_sum8(ws, nseg, stride, N, row, n0 + 128 + j, u);
-      p.apply<8>(row, (n0 / 256) * 128 + j, g, u);
-    }
-  }
-};
-
-template <class Fin>
-struct EpiStreamK {
-  int M, N;
-  float* ws;       // [slots][M][N] fp32
-  int* counters;   // [tiles], zero before the first launch, left zero after
-  int kblocks, per;
-  Fin fin;
-  __device__ void operator()(const gemm::EpiCtx& c) const {
-#pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 32) {
-      float v[32];
-      gemm::tmem_ld32(c.taddr + c0, v);
-      if (!c.row_ok || c.n0 + c0 >= N) continue;
-      gemm::store_row32(ws + (int64_t)c.ks * M * N, N, 1, c.row, c.n0 + c0, N, v);
-    }
-    const int t = c.n0 / 256;
-    const int first = (int)(((long long)t * kblocks) / per);
-    const int last = (int)(((long long)(t + 1) * kblocks - 1) / per);
-    const int nseg = last - first + 1;
-    __shared__ int s_last;
-    __threadfence();  // my partial is visible before the arrival is counted
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
-    if (threadIdx.x == 128) {
-      const int prev = atomicAdd(&counters[t], 1);
-      s_last = prev == nseg - 1;
-      if (s_last) counters[t] = 0;
-    }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (!s_last) return;
-    __threadfence();
-    fin.finish(ws, nseg, (int64_t)M * N, M, N, c.n0, (int)threadIdx.x - 128, 128);
-  }
-};
-
-}  // namespace dec

@@ -374,10 +374,7 @@ __global__ void __launch_bounds__(256, 1)
     for (; sched.next(cur, tm, tn, ks, kb0, kb1); ++i) {
       const int buf = i & 1;
       const uint32_t tph = (i >> 1) & 1;
-      const bool got = mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag);
-      // the four epilogue warps continue or stop together (epilogues may use
-      // named barrier 1 among themselves)
-      if (!mbd::vote_all(got, 2, 128)) break;
+      if (!mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag)) break;
       mbd::tc_fence_after();
       EpiCtx c;
       c.taddr = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
