@@ -120,6 +120,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// AND of `ok` over the `nthreads` threads that reach named barrier `id`; all of
+// them get the same answer, so they can leave a loop together (no thread is
+// left waiting at a later barrier for one that already left).
+__device__ __forceinline__ bool vote_all(bool ok, int id, int nthreads) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // 2-D tiled TMA load global -> shared, completion on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {

@@ -374,7 +374,10 @@ __global__ void __launch_bounds__(256, 1)
     for (; sched.next(cur, tm, tn, ks, kb0, kb1); ++i) {
       const int buf = i & 1;
       const uint32_t tph = (i >> 1) & 1;
-      if (!mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag)) break;
+      const bool got = mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag);
+      // the four epilogue warps continue or stop together, so an epilogue may
+      // use a named barrier among them
+      if (!mbd::vote_all(got, 2, 128)) break;
       mbd::tc_fence_after();
       EpiCtx c;
       c.taddr = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
