@@ -232,6 +232,37 @@ int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, 
 /* In-place bf16 sum all-reduce over the tensor-parallel communicator. */
 int mb_tp_allreduce_bf16(uint16_t* buf, size_t count, void* stream);
 
+/* ---- standard-set fused ops (mlx/kernels/standard/registry.py:26-42,
+ *      103-132, 280-292, 382-396; hooks mlx/kernels/standard/*.py) -------- */
+
+/* y[M,N] = rms_norm(x[M,K]) @ w^T with w [N, K] (rms_norm_linear.py); the
+ * norm is a per-row scale of the GEMM epilogue. Workspace: M floats. */
+size_t mb_rms_norm_linear_workspace_bytes(int64_t M);
+int mb_rms_norm_linear_bf16(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t M, int64_t K,
+                            int64_t N, float eps, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* y = rms_norm(x + residual), rows of D (fused_add_rms_norm.py). */
+int mb_fused_add_rms_norm_bf16(const uint16_t* x, const uint16_t* residual, uint16_t* y, int64_t M,
+                               int64_t D, float eps, void* stream);
+
+/* Interleaved-pair RoPE of [S, D] at positions 0..S-1, omega_i = base^(-2i/D)
+ * (rope_embedding.py). */
+int mb_rope_bf16(const uint16_t* x, uint16_t* y, int64_t S, int64_t D, float base, void* stream);
+
+/* out[M, FF] = silu(x @ w_gate) * (x @ w_up) (swiglu.py): pack the two
+ * (in, out) [D, FF] weights once, then run the fused GEMM. */
+size_t mb_swiglu_packed_bytes(int64_t D, int64_t FF);
+int mb_swiglu_pack_bf16(const uint16_t* w_gate, const uint16_t* w_up, void* packed, int64_t D,
+                        int64_t FF, void* stream);
+int mb_swiglu_bf16(const uint16_t* x, const void* packed, uint16_t* out, int64_t M, int64_t D,
+                   int64_t FF, void* stream);
+
+/* O[S,128] = softmax(Q K^T / sqrt(128)) V, single head (scaled_dot_product.py). */
+size_t mb_sdpa_workspace_bytes(int64_t S);
+int mb_sdpa_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int64_t S,
+                 int64_t d, void* workspace, size_t workspace_bytes, void* stream);
+
 /* sqr_mm for callers that cannot allocate device memory. This entry point
  * has no counterpart in the reference. It computes exactly what
  * mb_sqr_mm_f32 computes, but takes its scratch from a 64 MiB array compiled

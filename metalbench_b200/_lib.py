@@ -87,6 +87,16 @@ SIGNATURES = {
     "mb_decoder_layer_forward": (C.c_int, [_P, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _I, _I, _P,
                                            C.c_size_t, _P]),
     "mb_tp_allreduce_bf16": (C.c_int, [_P, C.c_size_t, _P]),
+    "mb_rms_norm_linear_workspace_bytes": (C.c_size_t, [_I64]),
+    "mb_rms_norm_linear_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, C.c_float, _P,
+                                          C.c_size_t, _P]),
+    "mb_fused_add_rms_norm_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, C.c_float, _P]),
+    "mb_rope_bf16": (C.c_int, [_P, _P, _I64, _I64, C.c_float, _P]),
+    "mb_swiglu_packed_bytes": (C.c_size_t, [_I64, _I64]),
+    "mb_swiglu_pack_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
+    "mb_swiglu_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P]),
+    "mb_sdpa_workspace_bytes": (C.c_size_t, [_I64]),
+    "mb_sdpa_bf16": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _P, C.c_size_t, _P]),
     "mb_sqr_mm_f32_noalloc_max_workspace_bytes": (C.c_size_t, []),
     "mb_sqr_mm_f32_noalloc": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P]),
 }

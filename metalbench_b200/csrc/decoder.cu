@@ -193,6 +193,34 @@ __global__ void tile_weights_kernel(const uint16_t* __restrict__ w, int64_t N, i
 }
 
 
+// Direct pack into the tiled, pre-swizzled layout: 16-byte chunk c of row r of
+// tile (tn, kb) gathers in[(kb*64 + c*8 + j) * ld_in + col_idx[tn*256 + r]],
+// j = 0..7 (rows past Nout are zero). One-time weight preparation.
+__global__ void pack_tiled_kernel(const uint16_t* __restrict__ in, int64_t ld_in, int K,
+                                  const int* __restrict__ col_idx, int Nout,
+                                  uint8_t* __restrict__ out) {
+  const int64_t kblocks = K / 64, tiles_n = (Nout + 255) / 256;
+  const int64_t chunks = tiles_n * kblocks * 256 * 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < chunks;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tile = i / (256 * 8);
+    const int r = (int)((i / 8) % 256), c = (int)(i % 8);
+    const int64_t tn = tile / kblocks, kb = tile % kblocks;
+    const int64_t n = tn * 256 + r;
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (n < Nout) {
+      const int64_t col = col_idx[n];
+      const int64_t k0 = kb * 64 + c * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        w[j] = (uint32_t)in[(k0 + 2 * j) * ld_in + col] |
+               ((uint32_t)in[(k0 + 2 * j + 1) * ld_in + col] << 16);
+    }
+    *reinterpret_cast<uint4*>(out + tile * (256 * gemm::KBYTES) + r * gemm::KBYTES +
+                              ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // out[n][k] = in[k * ld_in + col_idx[n]] for k < K: packs selected columns of a
 // row-major (in, out) weight into a K-major [n, K] operand (32x32 smem tiles).
 __global__ void pack_cols_kernel(const uint16_t* __restrict__ in, int64_t ld_in, int K,
@@ -352,6 +380,23 @@ unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256);
 
 
 }  // namespace
+
+namespace mb {
+// Shared with the standalone fused ops (fused_ops.cu).
+int rownorm(const uint16_t* x, int M, int D, float eps, float* rstd, cudaStream_t s) {
+  MB_REQUIRE(D % 8 == 0, "rownorm: D must be a multiple of 8");
+  rownorm_kernel<<<(unsigned)((M + 7) / 8), 256, 0, s>>>(x, M, D, eps, rstd);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+int pack_tiled_weight(const uint16_t* in, int64_t ld_in, int K, const int* col_idx_dev, int Nout,
+                      uint8_t* out, cudaStream_t s) {
+  MB_REQUIRE(K % 64 == 0, "weight packing: K must be a multiple of 64");
+  pack_tiled_kernel<<<1024, 256, 0, s>>>(in, ld_in, K, col_idx_dev, Nout, out);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+}  // namespace mb
 
 extern "C" int mb_decoder_layer_create(const mb_decoder_config* cfg, const uint16_t* W_qkv,
                                        const uint16_t* W_o, const uint16_t* W_gu,

@@ -1,0 +1,210 @@
+// Standalone fused ops: the sub-steps of the decoder as their own registry
+// kernels (reference standard set, mlx/kernels/standard/registry.py).
+//
+//   mb_rms_norm_linear_bf16     y = rms_norm(x) @ w^T   (rms_norm_linear.py; w [N, K])
+//   mb_fused_add_rms_norm_bf16  y = rms_norm(x + r)     (fused_add_rms_norm.py)
+//   mb_rope_bf16                interleaved-pair RoPE over the full width
+//                               (rope_embedding.py: omega_i = base^(-2i/D))
+//   mb_swiglu_*                 silu(x @ Wg) * (x @ Wu)   (swiglu.py)
+//   mb_sdpa_bf16                softmax(Q K^T / sqrt(d)) V  (scaled_dot_product.py)
+//
+// They reuse the decoder's pieces: the row-norm kernel, the tcgen05 GEMM core
+// with its row-scale and SwiGLU epilogues, and the paged attention kernel (a
+// contiguous [S, 128] K or V is a valid page sequence with an identity page
+// table).
+#include "decoder_epi.cuh"
+#include "gemm_launch.cuh"
+#include "kernels.h"
+
+namespace {
+
+using namespace gemm;
+
+// y = (x + r) * rsqrt(mean((x + r)^2) + eps), one warp per row, fp32 math.
+__global__ void add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ r,
+                                    uint16_t* __restrict__ y, int M, int D, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const uint4* xp = reinterpret_cast<const uint4*>(x + (int64_t)row * D);
+  const uint4* rp = reinterpret_cast<const uint4*>(r + (int64_t)row * D);
+  float ss = 0.f;
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 a = xp[c], b = rp[c];
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float s0 = __uint_as_float(aw[m] << 16) + __uint_as_float(bw[m] << 16);
+      const float s1 = __uint_as_float(aw[m] & 0xFFFF0000u) + __uint_as_float(bw[m] & 0xFFFF0000u);
+      ss += s0 * s0 + s1 * s1;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rs = rsqrtf(ss / (float)D + eps);
+  uint4* yp = reinterpret_cast<uint4*>(y + (int64_t)row * D);
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 a = xp[c], b = rp[c];
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float s0 = (__uint_as_float(aw[m] << 16) + __uint_as_float(bw[m] << 16)) * rs;
+      const float s1 =
+          (__uint_as_float(aw[m] & 0xFFFF0000u) + __uint_as_float(bw[m] & 0xFFFF0000u)) * rs;
+      o[m] = gemm::pack_bf16(s0, s1);
+    }
+    yp[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// RoPE over the full width: thread per (position s, pair i).
+__global__ void rope_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int S, int D,
+                            float neg_log2_base_over_half) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int half = D / 2;
+  if (t >= (int64_t)S * half) return;
+  const int s = (int)(t / half), i = (int)(t % half);
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(x + (int64_t)s * D + 2 * i);
+  const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xFFFF0000u);
+  float sn, cs;
+  sincosf((float)s * exp2f(neg_log2_base_over_half * (float)i), &sn, &cs);
+  *reinterpret_cast<uint32_t*>(y + (int64_t)s * D + 2 * i) =
+      gemm::pack_bf16(a * cs - b * sn, a * sn + b * cs);
+}
+
+// Pack W_gate, W_up (both [D, FF], reference (in, out) layout) into the tiled,
+// pre-swizzled K-major layout of the decoder's gate/up GEMM: column block t of
+// 256 packed rows = gate features t*128.. then the matching up features.
+__global__ void swiglu_pack_kernel(const uint16_t* __restrict__ wg, const uint16_t* __restrict__ wu,
+                                   int D, int FF, uint8_t* __restrict__ out) {
+  const int64_t kblocks = D / 64, tiles_n = (2 * (int64_t)FF + 255) / 256;
+  const int64_t chunks = tiles_n * kblocks * 256 * 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < chunks;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tile = i / (256 * 8);
+    const int r = (int)((i / 8) % 256), c = (int)(i % 8);
+    const int64_t tn = tile / kblocks, kb = tile % kblocks;
+    const uint16_t* src = r < 128 ? wg : wu;
+    const int64_t col = tn * 128 + (r % 128);
+    const int64_t k0 = kb * 64 + c * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = (uint32_t)src[(k0 + 2 * j) * FF + col] | ((uint32_t)src[(k0 + 2 * j + 1) * FF + col] << 16);
+    *reinterpret_cast<uint4*>(out + tile * (256 * KBYTES) + r * KBYTES + ((c ^ (r & 7)) * 16)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__global__ void sdpa_tables_kernel(int* bt, int pages, int* start_pos, int* kv_len, int S) {
+  for (int i = threadIdx.x; i < pages; i += blockDim.x) bt[i] = i;
+  if (threadIdx.x == 0) {
+    start_pos[0] = 0;
+    kv_len[0] = S;
+  }
+}
+
+}  // namespace
+
+extern "C" size_t mb_rms_norm_linear_workspace_bytes(int64_t M) {
+  return M > 0 ? (size_t)((M * 4 + 255) / 256 * 256) : 0;
+}
+
+extern "C" int mb_rms_norm_linear_bf16(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t M,
+                                       int64_t K, int64_t N, float eps, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  MB_REQUIRE(M >= 0 && K > 0 && N >= 0, "rms_norm_linear: bad sizes");
+  if (M == 0 || N == 0) return MB_OK;
+  MB_REQUIRE(K % 8 == 0 && N % 8 == 0, "rms_norm_linear: K and N must be multiples of 8");
+  MB_REQUIRE(workspace && workspace_bytes >= mb_rms_norm_linear_workspace_bytes(M),
+             "rms_norm_linear: workspace of %zu bytes required",
+             mb_rms_norm_linear_workspace_bytes(M));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* rstd = static_cast<float*>(workspace);
+  int rc = mb::rownorm(x, (int)M, (int)K, eps, rstd, s);
+  if (rc) return rc;
+  Epi<256, EpiStore> e{};
+  e.M = (int)M;
+  e.N = (int)N;
+  e.out = y;
+  e.ldo = N;
+  e.alpha = 1.f;
+  e.row_scale = rstd;
+  return launch_gemm<Mode::BF16, 256, 4, false>(x, w, e, M, N, K, 1, s);
+}
+
+extern "C" int mb_fused_add_rms_norm_bf16(const uint16_t* x, const uint16_t* residual,
+                                          uint16_t* y, int64_t M, int64_t D, float eps,
+                                          void* stream) {
+  MB_REQUIRE(M >= 0 && D > 0 && D % 8 == 0, "fused_add_rms_norm: D must be a multiple of 8");
+  if (M == 0) return MB_OK;
+  add_rms_norm_kernel<<<(unsigned)((M + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, residual, y, (int)M, (int)D, eps);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+extern "C" int mb_rope_bf16(const uint16_t* x, uint16_t* y, int64_t S, int64_t D, float base,
+                            void* stream) {
+  MB_REQUIRE(S >= 0 && D > 0 && D % 2 == 0, "rope: D must be even");
+  if (S == 0) return MB_OK;
+  const int64_t n = S * (D / 2);
+  rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, (int)S, (int)D, -log2f(base) / (float)(D / 2));
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+extern "C" size_t mb_swiglu_packed_bytes(int64_t D, int64_t FF) {
+  if (D <= 0 || FF <= 0) return 0;
+  return gemm::tiled_weight_bytes(2 * FF, D, 256);
+}
+
+extern "C" int mb_swiglu_pack_bf16(const uint16_t* w_gate, const uint16_t* w_up, void* packed,
+                                   int64_t D, int64_t FF, void* stream) {
+  MB_REQUIRE(D > 0 && D % 64 == 0 && FF > 0 && FF % 128 == 0,
+             "swiglu pack: D %% 64 == 0 and FF %% 128 == 0 required");
+  swiglu_pack_kernel<<<1024, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w_gate, w_up, (int)D, (int)FF, static_cast<uint8_t*>(packed));
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+extern "C" int mb_swiglu_bf16(const uint16_t* x, const void* packed, uint16_t* out, int64_t M,
+                              int64_t D, int64_t FF, void* stream) {
+  MB_REQUIRE(M >= 0 && D % 64 == 0 && FF % 128 == 0, "swiglu: D %% 64 and FF %% 128 required");
+  if (M == 0) return MB_OK;
+  dec::EpiSwiGLU e;
+  e.M = (int)M;
+  e.p.M = (int)M;
+  e.p.FF = (int)FF;
+  e.p.rstd = nullptr;
+  e.p.act = out;
+  return launch_gemm<Mode::BF16, 256, 4, false>(x, packed, e, M, 2 * FF, D, 1,
+                                                static_cast<cudaStream_t>(stream), false, true);
+}
+
+extern "C" size_t mb_sdpa_workspace_bytes(int64_t S) {
+  if (S <= 0) return 0;
+  return (size_t)(((S + 63) / 64 + 2) * 4 + 255) / 256 * 256;
+}
+
+extern "C" int mb_sdpa_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
+                            int64_t S, int64_t d, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  MB_REQUIRE(d == 128, "sdpa: head dimension must be 128");
+  MB_REQUIRE(S >= 0 && S <= (1 << 24), "sdpa: bad S");
+  if (S == 0) return MB_OK;
+  MB_REQUIRE(workspace && workspace_bytes >= mb_sdpa_workspace_bytes(S),
+             "sdpa: workspace of %zu bytes required", mb_sdpa_workspace_bytes(S));
+  const int pages = (int)((S + 63) / 64);
+  int* bt = static_cast<int*>(workspace);
+  int* sp = bt + pages;
+  int* kl = sp + 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  sdpa_tables_kernel<<<1, 256, 0, s>>>(bt, pages, sp, kl, (int)S);
+  MB_CUDA(cudaGetLastError());
+  // [S, 128] rows are pages of 64 keys for one kv head: an identity page table
+  return mb_attention_prefill_bf16(Q, 128, K, V, bt, pages, sp, kl, 1, (int)S, 1, 1, 128, 0, O,
+                                   128, stream);
+}

@@ -62,4 +62,9 @@ int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream);
 int tp_world();
 int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 
+// decoder.cu helpers shared with fused_ops.cu
+int rownorm(const uint16_t* x, int M, int D, float eps, float* rstd, cudaStream_t s);
+int pack_tiled_weight(const uint16_t* in, int64_t ld_in, int K, const int* col_idx_dev, int Nout,
+                      uint8_t* out, cudaStream_t s);
+
 }  // namespace mb

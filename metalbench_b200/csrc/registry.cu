@@ -2,6 +2,7 @@
 // the device-pointer entry points. Binding numbers follow the reference
 // registry entries (mlx/kernels/common/registry.py, mlx/kernels/full/registry.py).
 #include <mutex>
+#include <initializer_list>
 #include <vector>
 
 #include "common.cuh"
@@ -273,6 +274,150 @@ int prep_llama(const RunArgs& a, KernelState& st, cudaStream_t stream) {
   return MB_OK;
 }
 
+int bf16_all(const std::initializer_list<const RunArgs::Buf*>& bl, const char* what) {
+  for (const RunArgs::Buf* b : bl)
+    MB_REQUIRE(b->dtype == MB_BF16, "%s: buffers must be bf16", what);
+  return MB_OK;
+}
+
+// rms_norm_linear: standard/registry.py:26-42 — x@0 [M,K], w@1 [N,K], y@2;
+// M@3, N@4, K@5, eps@6 (f32).
+int prep_rms_norm_linear(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *w, *y;
+  int64_t M, N, K;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &w));
+  TRY(need_buf(a, 2, MB_ROLE_OUTPUT, &y));
+  TRY(need_scalar(a, 3, &M));
+  TRY(need_scalar(a, 4, &N));
+  TRY(need_scalar(a, 5, &K));
+  double eps = 1e-5;
+  a.scalar(6, &eps);
+  TRY(bf16_all({x, w, y}, "rms_norm_linear"));
+  MB_REQUIRE(x->bytes == (size_t)(M * K * 2) && w->bytes == (size_t)(N * K * 2) &&
+                 y->bytes == (size_t)(M * N * 2),
+             "rms_norm_linear: buffer sizes do not match M/N/K");
+  const size_t wsb = mb_rms_norm_linear_workspace_bytes(M);
+  void* ws = nullptr;
+  MB_CUDA(cudaMalloc(&ws, wsb));
+  st.scratch.push_back(ws);
+  const void *px = x->dev, *pw = w->dev;
+  void* py = y->dev;
+  st.launches_per_iter = 2;
+  st.launch = [=](cudaStream_t s) {
+    return mb_rms_norm_linear_bf16((const uint16_t*)px, (const uint16_t*)pw, (uint16_t*)py, M, K,
+                                   N, (float)eps, ws, wsb, s);
+  };
+  return MB_OK;
+}
+
+// fused_add_rms_norm: standard/registry.py:280-292 — x@0, residual@1, y@2;
+// D@3, eps@4 (f32); rows = size / D.
+int prep_add_rms_norm(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *r, *y;
+  int64_t D;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &r));
+  TRY(need_buf(a, 2, MB_ROLE_OUTPUT, &y));
+  TRY(need_scalar(a, 3, &D));
+  double eps = 1e-5;
+  a.scalar(4, &eps);
+  TRY(bf16_all({x, r, y}, "fused_add_rms_norm"));
+  MB_REQUIRE(D > 0 && x->bytes % (size_t)(D * 2) == 0 && r->bytes == x->bytes &&
+                 y->bytes == x->bytes,
+             "fused_add_rms_norm: buffer sizes do not match D");
+  const int64_t M = (int64_t)(x->bytes / (D * 2));
+  const void *px = x->dev, *pr = r->dev;
+  void* py = y->dev;
+  st.launch = [=](cudaStream_t s) {
+    return mb_fused_add_rms_norm_bf16((const uint16_t*)px, (const uint16_t*)pr, (uint16_t*)py, M,
+                                      D, (float)eps, s);
+  };
+  return MB_OK;
+}
+
+// rope_embedding: standard/registry.py:103-116 — x@0 [S,D], y@1; S@2, D@3, base@4.
+int prep_rope(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *y;
+  int64_t S, D;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_OUTPUT, &y));
+  TRY(need_scalar(a, 2, &S));
+  TRY(need_scalar(a, 3, &D));
+  double base = 10000.0;
+  a.scalar(4, &base);
+  TRY(bf16_all({x, y}, "rope_embedding"));
+  MB_REQUIRE(x->bytes == (size_t)(S * D * 2) && y->bytes == x->bytes,
+             "rope_embedding: buffer sizes do not match S/D");
+  const void* px = x->dev;
+  void* py = y->dev;
+  st.launch = [=](cudaStream_t s) {
+    return mb_rope_bf16((const uint16_t*)px, (uint16_t*)py, S, D, (float)base, s);
+  };
+  return MB_OK;
+}
+
+// swiglu: standard/registry.py:119-132 — x@0 [M,D], w_gate@1 [D,FF], w_up@2,
+// out@3 [M,FF]; M@4, D@5, FF@6. The weights are packed in prepare (untimed).
+int prep_swiglu(const RunArgs& a, KernelState& st, cudaStream_t stream) {
+  const RunArgs::Buf *x, *wg, *wu, *y;
+  int64_t M, D, FF;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &wg));
+  TRY(need_buf(a, 2, MB_ROLE_INPUT, &wu));
+  TRY(need_buf(a, 3, MB_ROLE_OUTPUT, &y));
+  TRY(need_scalar(a, 4, &M));
+  TRY(need_scalar(a, 5, &D));
+  TRY(need_scalar(a, 6, &FF));
+  TRY(bf16_all({x, wg, wu, y}, "swiglu"));
+  MB_REQUIRE(x->bytes == (size_t)(M * D * 2) && wg->bytes == (size_t)(D * FF * 2) &&
+                 wu->bytes == wg->bytes && y->bytes == (size_t)(M * FF * 2),
+             "swiglu: buffer sizes do not match M/D/FF");
+  const size_t pb = mb_swiglu_packed_bytes(D, FF);
+  void* packed = nullptr;
+  MB_CUDA(cudaMalloc(&packed, pb));
+  st.scratch.push_back(packed);
+  TRY(mb_swiglu_pack_bf16((const uint16_t*)wg->dev, (const uint16_t*)wu->dev, packed, D, FF,
+                          stream));
+  MB_CUDA(cudaStreamSynchronize(stream));
+  const void* px = x->dev;
+  void* py = y->dev;
+  st.threads_per_cta = 256;
+  st.launch = [=](cudaStream_t s) {
+    return mb_swiglu_bf16((const uint16_t*)px, packed, (uint16_t*)py, M, D, FF, s);
+  };
+  return MB_OK;
+}
+
+// scaled_dot_product: standard/registry.py:382-396 — Q@0, K@1, V@2 [S,d], O@3;
+// S@4, d@5.
+int prep_sdpa(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *q, *k, *v, *o;
+  int64_t S, d;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &q));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &k));
+  TRY(need_buf(a, 2, MB_ROLE_INPUT, &v));
+  TRY(need_buf(a, 3, MB_ROLE_OUTPUT, &o));
+  TRY(need_scalar(a, 4, &S));
+  TRY(need_scalar(a, 5, &d));
+  TRY(bf16_all({q, k, v, o}, "scaled_dot_product"));
+  MB_REQUIRE(q->bytes == (size_t)(S * d * 2) && k->bytes == q->bytes && v->bytes == q->bytes &&
+                 o->bytes == q->bytes,
+             "scaled_dot_product: buffer sizes do not match S/d");
+  const size_t wsb = mb_sdpa_workspace_bytes(S);
+  void* ws = nullptr;
+  MB_CUDA(cudaMalloc(&ws, wsb));
+  st.scratch.push_back(ws);
+  const void *pq = q->dev, *pk = k->dev, *pv = v->dev;
+  void* po = o->dev;
+  st.launches_per_iter = 2;
+  st.launch = [=](cudaStream_t s) {
+    return mb_sdpa_bf16((const uint16_t*)pq, (const uint16_t*)pk, (const uint16_t*)pv,
+                        (uint16_t*)po, S, d, ws, wsb, s);
+  };
+  return MB_OK;
+}
+
 }  // namespace
 
 void register_all_kernels() {
@@ -284,6 +429,11 @@ void register_all_kernels() {
     register_kernel({"gemm_bf16", prep_gemm_bf16});
     register_kernel({"conv2d", prep_conv2d});
     register_kernel({"llama_decoder_layer", prep_llama});
+    register_kernel({"rms_norm_linear", prep_rms_norm_linear});
+    register_kernel({"fused_add_rms_norm", prep_add_rms_norm});
+    register_kernel({"rope_embedding", prep_rope});
+    register_kernel({"swiglu", prep_swiglu});
+    register_kernel({"scaled_dot_product", prep_sdpa});
   });
 }
 

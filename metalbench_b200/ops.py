@@ -145,3 +145,74 @@ def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, stride: int = 1, padding: int 
     _lib.call("mb_conv2d_nhwc_bf16", x.data_ptr(), w.data_ptr(), out.data_ptr(), N, H, W, C, Co,
               KH, KW, stride, padding, _stream())
     return out
+
+
+def rms_norm_linear(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """y = rms_norm(x) @ w.T for bf16 x [M, K], w [N, K]."""
+    _cuda(x, "rms_norm_linear(x)", (torch.bfloat16,))
+    _cuda(w, "rms_norm_linear(w)", (torch.bfloat16,))
+    init(x.device.index)
+    M, K = x.shape
+    N = w.shape[0]
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    nb = _lib.lib().mb_rms_norm_linear_workspace_bytes(M)
+    ws = _workspace(nb, x.device)
+    _lib.call("mb_rms_norm_linear_bf16", x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K, N, eps,
+              ws.data_ptr(), nb, _stream())
+    return y
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    _cuda(x, "fused_add_rms_norm(x)", (torch.bfloat16,))
+    _cuda(residual, "fused_add_rms_norm(residual)", (torch.bfloat16,))
+    init(x.device.index)
+    y = torch.empty_like(x)
+    _lib.call("mb_fused_add_rms_norm_bf16", x.data_ptr(), residual.data_ptr(), y.data_ptr(),
+              x.numel() // x.shape[-1], x.shape[-1], eps, _stream())
+    return y
+
+
+def rope(x: torch.Tensor, base: float = 10000.0) -> torch.Tensor:
+    """Interleaved-pair RoPE of x [S, D] at positions 0..S-1 over the full width."""
+    _cuda(x, "rope(x)", (torch.bfloat16,))
+    init(x.device.index)
+    y = torch.empty_like(x)
+    _lib.call("mb_rope_bf16", x.data_ptr(), y.data_ptr(), x.shape[0], x.shape[1], base, _stream())
+    return y
+
+
+def swiglu_pack(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    _cuda(w_gate, "swiglu_pack(w_gate)", (torch.bfloat16,))
+    _cuda(w_up, "swiglu_pack(w_up)", (torch.bfloat16,))
+    init(w_gate.device.index)
+    D, FF = w_gate.shape
+    packed = torch.empty(_lib.lib().mb_swiglu_packed_bytes(D, FF), dtype=torch.uint8,
+                         device=w_gate.device)
+    _lib.call("mb_swiglu_pack_bf16", w_gate.data_ptr(), w_up.data_ptr(), packed.data_ptr(), D, FF,
+              _stream())
+    return packed
+
+
+def swiglu(x: torch.Tensor, packed: torch.Tensor, ffn: int) -> torch.Tensor:
+    """silu(x @ w_gate) * (x @ w_up) with weights from swiglu_pack."""
+    _cuda(x, "swiglu(x)", (torch.bfloat16,))
+    init(x.device.index)
+    M, D = x.shape
+    out = torch.empty((M, ffn), dtype=torch.bfloat16, device=x.device)
+    _lib.call("mb_swiglu_bf16", x.data_ptr(), packed.data_ptr(), out.data_ptr(), M, D, ffn,
+              _stream())
+    return out
+
+
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """softmax(q k^T / sqrt(128)) v for one head, [S, 128] bf16."""
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _cuda(t, f"sdpa({n})", (torch.bfloat16,))
+    init(q.device.index)
+    S = q.shape[0]
+    o = torch.empty_like(q)
+    nb = _lib.lib().mb_sdpa_workspace_bytes(S)
+    ws = _workspace(nb, q.device)
+    _lib.call("mb_sdpa_bf16", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), S,
+              q.shape[1], ws.data_ptr(), nb, _stream())
+    return o

@@ -71,3 +71,14 @@ REGISTRY["gemm_bf16"] = dict(
     config={"b_layout": 1}, hook="sqr_mm",
     rtol=2e-2, atol=2.0, seed=4, flops=2 * 4096 ** 3, bytes=3 * 4096 * 4096 * 2,
     roof="tensor_bf16", ref_warmup=1, ref_iters=3)
+
+REGISTRY["rect_mm"] = dict(
+    kernel="sqr_mm", metal_function="rect_matmul_f32",
+    input_bindings=(0, 1), input_shapes=[(1024, 4096), (4096, 2048)],
+    input_dtypes=["f32", "f32"], input_init=[("normal", 1.0), ("normal", 1.0)],
+    output_shape=(1024, 2048), output_dtype="f32",
+    scalars=[dict(binding=3, dtype="u32", value=1024), dict(binding=4, dtype="u32", value=2048),
+             dict(binding=5, dtype="u32", value=4096)],
+    rtol=1e-4, atol=1e-3, seed=0, flops=2 * 1024 * 2048 * 4096,
+    bytes=4 * (1024 * 4096 + 4096 * 2048 + 1024 * 2048),
+    roof="tensor_tf32x3", ref_warmup=1, ref_iters=5)

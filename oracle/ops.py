@@ -232,3 +232,43 @@ def allclose_report(actual, expected, rtol: float, atol: float) -> dict:
     denom = np.maximum(np.abs(b), 1e-30)
     return {"all": bool(ok.all()), "frac_within_tol": float(ok.mean()),
             "max_err": float(np.nanmax(diff)), "max_rel_err": float(np.nanmax(diff / denom))}
+
+
+# ----------------------------------------------------------------------------
+# standard set (sub-steps of the decoder)
+# ----------------------------------------------------------------------------
+
+
+def rms_norm_linear(x, w, eps=1e-5, acc=np.float64):
+    """rms_norm(x) @ w.T, w stored (out_dim, dim)
+    (mlx/kernels/standard/rms_norm_linear.py:8-17)."""
+    xa = x.astype(acc)
+    return (rms_norm(xa, eps) @ w.astype(acc).T).astype(np.float32)
+
+
+def fused_add_rms_norm(x, residual, eps=1e-5, acc=np.float64):
+    """RMSNorm(x + residual) with unit gain
+    (mlx/kernels/standard/fused_add_rms_norm.py:6-13)."""
+    return rms_norm(x.astype(acc) + residual.astype(acc), eps).astype(np.float32)
+
+
+def rope_full(x, base=10000.0, acc=np.float64):
+    """Interleaved-pair RoPE over the full width of x (S, D), positions 0..S-1,
+    omega_i = base^(-2i/D) (mlx/kernels/standard/rope_embedding.py:14-30)."""
+    return rope(x.astype(acc), np.arange(x.shape[0]), base).astype(np.float32)
+
+
+def swiglu(x, w_gate, w_up, acc=np.float64):
+    """silu(x @ w_gate) * (x @ w_up) (mlx/kernels/standard/swiglu.py:10-11)."""
+    xa = x.astype(acc)
+    return (silu(xa @ w_gate.astype(acc)) * (xa @ w_up.astype(acc))).astype(np.float32)
+
+
+def sdpa(Q, K, V, acc=np.float64):
+    """softmax(Q K^T / sqrt(d)) V for one head
+    (mlx/kernels/standard/scaled_dot_product.py:9-14)."""
+    q, k, v = Q.astype(acc), K.astype(acc), V.astype(acc)
+    s = q @ k.T / np.sqrt(acc(q.shape[-1]))
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    return ((p / p.sum(axis=-1, keepdims=True)) @ v).astype(np.float32)

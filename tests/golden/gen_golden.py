@@ -35,6 +35,15 @@ CASES = [
     ("conv2d", "common", [(2, 10, 12, 64), (128, 3, 3, 64)], 2),
     ("llama_decoder_layer", "full",
      [(64, 128), (128, 128 + 2 * 2 * 32), (128, 128), (128, 2 * 256), (256, 128)], 3),
+    # standard set at the reference registry shapes (shrunk where large)
+    # (mlx/kernels/standard/registry.py:26-42, 103-132, 280-292, 324-337, 382-396)
+    ("rms_norm_linear", "standard", [(32, 1024), (48, 1024)], 5),
+    ("fused_add_rms_norm", "standard", [(16, 1024), (16, 1024)], 5),
+    ("rope_embedding", "standard", [(128, 64)], 5),
+    ("swiglu", "standard", [(32, 64), (64, 96), (64, 96)], 5),
+    ("scaled_dot_product", "standard", [(40, 128), (40, 128), (40, 128)], 5),
+    ("fused_qkv_projection", "standard", [(16, 64), (64, 48)], 5),
+    ("rect_mm", "common", [(32, 96), (96, 40)], 5),
 ]
 
 

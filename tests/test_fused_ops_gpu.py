@@ -1,0 +1,108 @@
+"""GPU parity of the standard-set fused ops against the float64 oracle on
+bf16-rounded inputs (mlx/kernels/standard/*.py hooks; oracle.ops restatements):
+every element within |a-b| <= 2e-2*|b| + 2e-2*rms(b), the bf16 tolerance of
+the registry entries."""
+import numpy as np
+import pytest
+
+import oracle.ops as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(torch, x):
+    return torch.from_numpy(O.f32_to_bf16(np.ascontiguousarray(x)).view(np.int16)).cuda().view(
+        torch.bfloat16)
+
+
+def _np(t):
+    import torch
+    return O.bf16_to_f32(t.view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def _check(got, ref, tol=2e-2):
+    atol = tol * float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)) or 1.0)
+    r = O.allclose_report(got, ref, rtol=tol, atol=atol)
+    assert r["all"], r
+
+
+def _r(rng, *s, scale=1.0):
+    return O.round_bf16((rng.standard_normal(s) * scale).astype(np.float32))
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 1024, 512), (100, 4096, 6144), (1, 64, 8),
+                                   (2048, 4096, 4096)])
+def test_rms_norm_linear(M, K, N):
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(10)
+    x, w = _r(rng, M, K), _r(rng, N, K, scale=K ** -0.5)
+    y = ops.rms_norm_linear(_bf(torch, x), _bf(torch, w))
+    _check(_np(y), O.rms_norm_linear(x, w))
+
+
+@pytest.mark.parametrize("M,D", [(8192, 4096), (3, 8), (17, 1000), (0, 64)])
+def test_fused_add_rms_norm(M, D):
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(11)
+    x, res = _r(rng, M, D), _r(rng, M, D)
+    y = ops.fused_add_rms_norm(_bf(torch, x), _bf(torch, res))
+    if M:
+        _check(_np(y), O.fused_add_rms_norm(x, res))
+
+
+@pytest.mark.parametrize("S,D", [(4096, 4096), (7, 6), (1, 2), (300, 128)])
+def test_rope(S, D):
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(12)
+    x = _r(rng, S, D)
+    y = ops.rope(_bf(torch, x))
+    _check(_np(y), O.rope_full(x))
+
+
+@pytest.mark.parametrize("M,D,FF", [(512, 1024, 1408), (8192, 4096, 14336), (1, 64, 128),
+                                    (300, 128, 256)])
+def test_swiglu(M, D, FF):
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(13)
+    if M * D * FF > 2 ** 31:  # torch fp32 reference of the same op for the full registry size
+        x, wg, wu = (torch.randn(M, D, device="cuda").bfloat16(),
+                     (torch.randn(D, FF, device="cuda") * D ** -0.5).bfloat16(),
+                     (torch.randn(D, FF, device="cuda") * D ** -0.5).bfloat16())
+        out = ops.swiglu(x, ops.swiglu_pack(wg, wu), FF)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        xf = x.float()
+        ref = torch.nn.functional.silu(xf @ wg.float()) * (xf @ wu.float())
+        _check(out.float().cpu().numpy(), ref.cpu().numpy())
+        return
+    x, wg, wu = _r(rng, M, D), _r(rng, D, FF, scale=D ** -0.5), _r(rng, D, FF, scale=D ** -0.5)
+    out = ops.swiglu(_bf(torch, x), ops.swiglu_pack(_bf(torch, wg), _bf(torch, wu)), FF)
+    _check(_np(out), O.swiglu(x, wg, wu))
+
+
+@pytest.mark.parametrize("S", [4096, 64, 1, 200, 1000])
+def test_sdpa(S):
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(14)
+    q, k, v = _r(rng, S, 128), _r(rng, S, 128), _r(rng, S, 128)
+    o = ops.sdpa(_bf(torch, q), _bf(torch, k), _bf(torch, v))
+    _check(_np(o), O.sdpa(q, k, v))
+
+
+def test_fused_qkv_projection_and_rect_mm_through_gemms():
+    """fused_qkv_projection is x @ [Wq|Wk|Wv] (bf16 gemm); rect_mm is the fp32
+    sqr_mm kernel on rectangular operands."""
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(15)
+    x, w = _r(rng, 512, 1024), _r(rng, 1024, 1536, scale=1024 ** -0.5)
+    _check(_np(ops.gemm_bf16(_bf(torch, x), _bf(torch, w), b_layout="kn")), O.sqr_mm(x, w))
+    A = rng.standard_normal((1000, 300)).astype(np.float32)
+    B = rng.standard_normal((300, 777)).astype(np.float32)
+    got = ops.sqr_mm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()).cpu().numpy()
+    ref = O.sqr_mm(A, B)
+    assert np.abs(got - ref).max() / np.abs(ref).max() <= 1e-4

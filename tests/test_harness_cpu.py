@@ -122,3 +122,17 @@ def test_grade_targets():
     m = {"speedup": 2.0, "gflops": 1000.0, "gbps": 5.0, "stability": 0.5}
     assert Hm.grade(m, "balanced") == pytest.approx(0.5 * 2 + 0.3 * 1 + 0.2 * 0.5)
     assert Hm.grade(m, "memory") == 5.0
+
+
+@pytest.mark.parametrize("name,nin", [("rms_norm_linear", 2), ("fused_add_rms_norm", 2),
+                                      ("rope_embedding", 1), ("swiglu", 3),
+                                      ("scaled_dot_product", 3), ("fused_qkv_projection", 2),
+                                      ("rect_mm", 2), ("sqr_mm", 2), ("transpose_2d", 1)])
+def test_our_hooks_reproduce_reference_hooks(name, nin):
+    """Each hook under mlx/kernels/ (default arguments) reproduces the golden
+    output of the reference's own hook on the same inputs."""
+    d = np.load(REPO / "tests" / "golden" / f"{name}.npz")
+    got = np.asarray(_hook(name).forward(*[d[f"in{i}"] for i in range(nin)]))
+    scale = max(1.0, float(np.abs(d["out"]).max()))
+    assert got.shape == d["out"].shape
+    assert np.abs(got - d["out"]).max() <= 1e-4 * scale, name

@@ -100,3 +100,19 @@ def test_allclose_report_fraction():
     b = np.array([1.0, 2.0, 3.5, 4.0])
     r = O.allclose_report(a, b, rtol=0.0, atol=0.1)
     assert not r["all"] and r["frac_within_tol"] == 0.75 and r["max_err"] == 0.5
+
+
+@pytest.mark.parametrize("name,fn", [
+    ("rms_norm_linear", lambda d: O.rms_norm_linear(d["in0"], d["in1"])),
+    ("fused_add_rms_norm", lambda d: O.fused_add_rms_norm(d["in0"], d["in1"])),
+    ("rope_embedding", lambda d: O.rope_full(d["in0"])),
+    ("swiglu", lambda d: O.swiglu(d["in0"], d["in1"], d["in2"])),
+    ("scaled_dot_product", lambda d: O.sdpa(d["in0"], d["in1"], d["in2"])),
+    ("fused_qkv_projection", lambda d: O.sqr_mm(d["in0"], d["in1"])),
+    ("rect_mm", lambda d: O.sqr_mm(d["in0"], d["in1"])),
+])
+def test_standard_set_oracle_matches_reference_hooks(name, fn):
+    d = _load(name)
+    got = fn(d)
+    scale = max(1.0, float(np.abs(d["out"]).max()))
+    assert np.abs(got - d["out"]).max() <= 1e-4 * scale, name
