@@ -30,6 +30,10 @@ extern "C" int mb_gemm_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, i
   return launch_gemm<gemm::Mode::BF16, 256, 4, true>(A, B, e, M, N, K, 1, s);
 }
 
+// k-blocks (32 fp32 of K each) per tensor-core partial sum of the 3xTF32
+// GEMM; the partial sums are added in fp32 registers (gemm_kernel PROMOTE).
+constexpr int kTf32PromoteBlocks = 4;
+
 namespace {
 
 // tf32 "hi" = the fp32 value with its low 13 mantissa bits cleared (exactly
@@ -137,7 +141,7 @@ extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M
   sc.kblocks = (int)((K + P::KE - 1) / P::KE);
   sc.ksplit = 1;
   sc.kb_per_split = sc.kblocks;
-  auto kern = gemm_kernel<128, 3, P, decltype(e)>;
+  auto kern = gemm_kernel<128, 3, P, decltype(e), kTf32PromoteBlocks>;
   static bool attr = false;
   if (!attr) {
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
@@ -255,7 +259,7 @@ extern "C" int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, i
   sc.kblocks = (int)((K + P::KE - 1) / P::KE);
   sc.ksplit = 1;
   sc.kb_per_split = sc.kblocks;
-  auto kern = gemm_kernel<128, 3, P, decltype(e)>;
+  auto kern = gemm_kernel<128, 3, P, decltype(e), kTf32PromoteBlocks>;
   MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
   const int grid = sc.total() < sms ? sc.total() : sms;
   kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, slot->status);

@@ -107,6 +107,19 @@ struct Sched {
   }
 };
 
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32_raw(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[16], t[16];
+  mbd::tmem_ld16(taddr, r);
+  mbd::tmem_ld16(taddr + 16, t);
+  mbd::tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    v[j] = __uint_as_float(r[j]);
+    v[16 + j] = __uint_as_float(t[j]);
+  }
+}
+
 // Epilogue context handed to the functor for one tile: the TMEM address of
 // this thread's row (lane) at column 0 of the accumulator, the global row,
 // the first global column, the split index and whether the row is in range.
@@ -250,7 +263,14 @@ struct DecodeProducer {
   }
 };
 
-template <int BN, int STAGES, class Producer, class Epi>
+// PROMOTE > 0: the accumulation is cut into chunks of PROMOTE k-blocks. Each
+// chunk is summed by the tensor core into a fresh TMEM accumulator and the
+// epilogue warps add the chunks in fp32 registers (round-to-nearest CUDA-core
+// adds), then call epi.store_acc(ctx, acc). The tensor core's own fp32
+// accumulation aligns the addends to the running sum and drops the bits below
+// it, so its error grows with the magnitude of the sum; restarting it every
+// chunk keeps that error at the level of a PROMOTE-block sum.
+template <int BN, int STAGES, class Producer, class Epi, int PROMOTE = 0>
 __global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ Producer prod, const __grid_constant__ Epi epi,
                 const Sched sched, uint32_t* status) {
@@ -340,26 +360,34 @@ __global__ void __launch_bounds__(256, 1)
       int i = 0;
       auto cur = sched.begin();
       int tm, tn, ks, kb0, kb1;
-      for (; ok && sched.next(cur, tm, tn, ks, kb0, kb1); ++i) {
-        const int buf = i & 1;
-        const uint32_t tph = (i >> 1) & 1;
-        if (!mbd::mbar_wait(&tempty[buf], tph ^ 1, status, MB_DEV_TIMEOUT_MMA, abort_flag)) break;
-        mbd::tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
+      while (ok && sched.next(cur, tm, tn, ks, kb0, kb1)) {
+        const int nch = PROMOTE > 0 ? (kb1 - kb0 + PROMOTE - 1) / PROMOTE : 1;
+        for (int ch = 0; ok && ch < nch; ++ch, ++i) {
+          const int ka = PROMOTE > 0 ? kb0 + ch * PROMOTE : kb0;
+          const int kz = PROMOTE > 0 ? min(kb1, ka + PROMOTE) : kb1;
+          const int buf = i & 1;
+          const uint32_t tph = (i >> 1) & 1;
+          if (!mbd::mbar_wait(&tempty[buf], tph ^ 1, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
             ok = false;
             break;
           }
           mbd::tc_fence_after();
-          prod.issue(d, mbd::smem_u32(sA(stage)), res_u32, kb, kb == kb0);
-          mbd::mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+          const uint32_t d = tmem + buf * BN;
+          for (int kb = ka; kb < kz; ++kb) {
+            if (!mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbd::tc_fence_after();
+            prod.issue(d, mbd::smem_u32(sA(stage)), res_u32, kb, kb == ka);
+            mbd::mma_commit(&empty[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
+          if (ok) mbd::mma_commit(&tfull[buf]);
         }
-        if (ok) mbd::mma_commit(&tfull[buf]);
       }
       // All MMAs issued by this thread are complete before TMEM is freed.
       mbd::mma_commit(drain);
@@ -371,23 +399,54 @@ __global__ void __launch_bounds__(256, 1)
     int i = 0;
     auto cur = sched.begin();
     int tm, tn, ks, kb0, kb1;
-    for (; sched.next(cur, tm, tn, ks, kb0, kb1); ++i) {
-      const int buf = i & 1;
-      const uint32_t tph = (i >> 1) & 1;
-      const bool got = mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag);
-      // the four epilogue warps continue or stop together, so an epilogue may
-      // use a named barrier among them
-      if (!mbd::vote_all(got, 2, 128)) break;
-      mbd::tc_fence_after();
+    bool ok = true;
+    while (ok && sched.next(cur, tm, tn, ks, kb0, kb1)) {
       EpiCtx c;
-      c.taddr = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
       c.row = tm * BM + q * 32 + lane;
       c.n0 = tn * BN;
       c.ks = ks;
       c.row_ok = c.row < epi.M;
-      epi(c);
-      mbd::tc_fence_before();
-      mbd::mbar_arrive(&tempty[buf]);
+      if constexpr (PROMOTE > 0) {
+        float acc[BN];
+#pragma unroll
+        for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+        const int nch = (kb1 - kb0 + PROMOTE - 1) / PROMOTE;
+        for (int ch = 0; ch < nch; ++ch, ++i) {
+          const int buf = i & 1;
+          const uint32_t tph = (i >> 1) & 1;
+          const bool got = mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag);
+          if (!mbd::vote_all(got, 2, 128)) {
+            ok = false;
+            break;
+          }
+          mbd::tc_fence_after();
+          const uint32_t ta = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+            tmem_ld32_raw(ta + c0, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[c0 + j] += v[j];
+          }
+          mbd::tc_fence_before();
+          mbd::mbar_arrive(&tempty[buf]);
+        }
+        if (!ok) break;
+        epi.store_acc(c, acc);
+      } else {
+        const int buf = i & 1;
+        const uint32_t tph = (i >> 1) & 1;
+        const bool got = mbd::mbar_wait(&tfull[buf], tph, status, MB_DEV_TIMEOUT_EPI, abort_flag);
+        // the four epilogue warps continue or stop together, so an epilogue may
+        // use a named barrier among them
+        if (!mbd::vote_all(got, 2, 128)) break;
+        mbd::tc_fence_after();
+        c.taddr = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
+        epi(c);
+        mbd::tc_fence_before();
+        mbd::mbar_arrive(&tempty[buf]);
+        ++i;
+      }
     }
   }
   __syncthreads();

@@ -105,37 +105,61 @@ struct EpiStore {
   const float* row_scale;
   const uint16_t* residual;  // bf16 [M, ld_res]
   int64_t ld_res;
+  // Scale, add the residual and store 32 accumulator values of row c.row
+  // starting at column n.
+  __device__ void finish32(const EpiCtx& c, float sc, int n, float (&v)[32]) const {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= sc;
+    if (residual) {
+      const uint16_t* r = residual + (int64_t)c.row * ld_res + n;
+      if (n + 32 <= N && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          const uint4 w = *reinterpret_cast<const uint4*>(r + j);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            v[j + 2 * m] += __uint_as_float(ws[m] << 16);
+            v[j + 2 * m + 1] += __uint_as_float(ws[m] & 0xFFFF0000u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n + j < N) v[j] += bf16_bits_to_f32(r[j]);
+      }
+    }
+    store_row32(out, ldo, out_f32, c.row, n, N, v);
+  }
+  __device__ float scale(const EpiCtx& c) const {
+    return (c.row_ok && row_scale) ? row_scale[c.row] * alpha : alpha;
+  }
   template <int BN>
   __device__ void run(const EpiCtx& c) const {
-    const float sc = (c.row_ok && row_scale) ? row_scale[c.row] * alpha : alpha;
+    const float sc = scale(c);
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
       float v[32];
       tmem_ld32(c.taddr + c0, v);
       const int n = c.n0 + c0;
       if (!c.row_ok || n >= N) continue;
+      finish32(c, sc, n, v);
+    }
+  }
+  // Same, from an accumulator the kernel summed in registers (PROMOTE mode).
+  template <int BN>
+  __device__ void run_acc(const EpiCtx& c, const float (&acc)[BN]) const {
+    if (!c.row_ok) return;
+    const float sc = scale(c);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] *= sc;
-      if (residual) {
-        const uint16_t* r = residual + (int64_t)c.row * ld_res + n;
-        if (n + 32 <= N && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      const int n = c.n0 + c0;
+      if (n < N) {
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            const uint4 w = *reinterpret_cast<const uint4*>(r + j);
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              v[j + 2 * m] += __uint_as_float(ws[m] << 16);
-              v[j + 2 * m + 1] += __uint_as_float(ws[m] & 0xFFFF0000u);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n + j < N) v[j] += bf16_bits_to_f32(r[j]);
-        }
+        for (int j = 0; j < 32; ++j) v[j] = acc[c0 + j];
+        finish32(c, sc, n, v);
       }
-      store_row32(out, ldo, out_f32, c.row, n, N, v);
     }
   }
 };
@@ -144,6 +168,9 @@ struct EpiStore {
 template <int BN, class E>
 struct Epi : E {
   __device__ void operator()(const EpiCtx& c) const { E::template run<BN>(c); }
+  __device__ void store_acc(const EpiCtx& c, const float (&acc)[BN]) const {
+    E::template run_acc<BN>(c, acc);
+  }
 };
 
 }  // namespace gemm

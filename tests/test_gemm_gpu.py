@@ -88,3 +88,19 @@ def test_gemm_device_status_clean():
     v = C.c_uint32(7)
     _lib.call("mb_device_status", C.byref(v))
     assert v.value == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 2048, 4096), (512, 512, 16384)])
+def test_sqr_mm_f32_elementwise_gate_deep_k(M, N, K):
+    """Every element within the registry's fp32 gate (|a-b| <= 1e-3 + 1e-4|b|)
+    of the float64 product, also at deep K: the tensor-core partial sums are
+    restarted every 128 of K and added in fp32 registers."""
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(6)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    got = ops.sqr_mm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()).cpu().numpy()
+    ref = A.astype(np.float64) @ B.astype(np.float64)
+    r = O.allclose_report(got, ref, rtol=1e-4, atol=1e-3)
+    assert r["all"], r
