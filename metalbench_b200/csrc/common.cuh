@@ -242,8 +242,10 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle.
 //  start address >> 4 in bits [0,14), leading byte offset >> 4 in [16,30),
 //  stride byte offset >> 4 in [32,46), version 1 at bit 46, layout type in
-//  [61,64) (2 = SWIZZLE_128B). Tiles are 1024-byte aligned, so the base offset
-//  field stays 0.
+//  [61,64) (2 = SWIZZLE_128B). The base offset field stays 0: the swizzle is a
+//  function of the shared-memory address bits, the same one TMA applies when
+//  it writes a 1024-byte-aligned box, so an operand may start at any 128-byte
+//  row of such a box (the conv2d producer starts taps at row r*TW + s).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes,
                                                uint32_t sbo_bytes) {
   uint64_t d = 0;

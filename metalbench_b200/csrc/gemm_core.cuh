@@ -21,6 +21,8 @@
 // tile i+1. Every mbarrier wait is bounded (common.cuh) and reports through
 // the device status word instead of hanging.
 #pragma once
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace gemm {
@@ -41,8 +43,34 @@ struct Smem {
   // barriers: full, empty per stage; tfull, tempty x2; resident;
   // then tmem slot, abort flag, drain barrier
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
-  static constexpr int TOTAL = 1024 /*alignment slack*/ + RES_BYTES + RING_BYTES + BAR_BYTES;
+  // work list (int4 per unit, Sched::MAX_LISTED of them), 16-byte aligned
+  static constexpr int WORK_OFF = (RES_BYTES + RING_BYTES + BAR_BYTES + 15) / 16 * 16;
+  static constexpr int WORK_BYTES = 16 * 64;
+  static constexpr int TOTAL = 1024 /*alignment slack*/ + WORK_OFF + WORK_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+};
+
+// Integer a / d for 0 <= a, d >= 1 without the ~20-instruction integer
+// division sequence: a float product with 1/d, then one correction step (the
+// estimate is off by at most one while a < 2^24; larger a divides exactly).
+// The schedule and epilogue index maths run on single threads whose latency
+// sits between consecutive tiles, so this matters for short tiles.
+struct FastDiv {
+  int d = 1;
+  float r = 1.f;
+  __host__ __device__ void set(int dd) {
+    d = dd;
+    r = 1.f / (float)dd;
+  }
+  __device__ __forceinline__ int div(int a) const {
+    if (a >= (1 << 24)) return a / d;
+    int q = (int)((float)a * r);
+    const int rem = a - q * d;
+    if (rem < 0) --q;
+    else if (rem >= d) ++q;
+    return q;
+  }
+  __device__ __forceinline__ int mod(int a) const { return a - div(a) * d; }
 };
 
 // Static tile list, rasterised in groups of GROUP_M tile-rows so that CTAs
@@ -50,17 +78,26 @@ struct Smem {
 struct Sched {
   int tiles_m, tiles_n, ksplit, kblocks, kb_per_split;
   static constexpr int GROUP_M = 16;
+  // reciprocals for get()/next(), filled on the device by init_fast()
+  FastDiv fd_ksplit, fd_group, fd_gm, fd_glast, fd_kblocks, fd_skper;
+  __device__ void init_fast() {
+    fd_ksplit.set(ksplit);
+    fd_group.set(GROUP_M * tiles_n);
+    fd_gm.set(GROUP_M);
+    fd_glast.set(tiles_m - (tiles_m - 1) / GROUP_M * GROUP_M);
+    fd_kblocks.set(kblocks);
+    fd_skper.set(sk_per > 0 ? sk_per : 1);
+  }
   __host__ __device__ int total() const { return tiles_m * tiles_n * ksplit; }
   __device__ void get(int t, int& tm, int& tn, int& ks) const {
-    ks = t % ksplit;
-    t /= ksplit;
-    const int per_group = GROUP_M * tiles_n;
-    const int g = t / per_group;
+    const int tq = fd_ksplit.div(t);
+    ks = t - tq * ksplit;
+    const int g = fd_group.div(tq);
     const int first = g * GROUP_M;
-    const int gsize = min(tiles_m - first, GROUP_M);
-    const int r = t % per_group;
-    tm = first + r % gsize;
-    tn = r / gsize;
+    const FastDiv& gs = tiles_m - first < GROUP_M ? fd_glast : fd_gm;
+    const int r = tq - g * fd_group.d;
+    tn = gs.div(r);
+    tm = first + r - tn * gs.d;
   }
   __device__ void krange(int ks, int& kb0, int& kb1) const {
     kb0 = ks * kb_per_split;
@@ -75,36 +112,36 @@ struct Sched {
   int streamk = 0;
   int sk_per = 0;
 
-  struct Cursor {
-    long long pos, end;
-    int t;
-  };
-  __device__ Cursor begin() const {
-    Cursor c;
-    c.t = blockIdx.x;
-    c.pos = (long long)blockIdx.x * sk_per;
-    c.end = streamk ? min(c.pos + sk_per, (long long)tiles_m * tiles_n * kblocks) : 0;
-    return c;
-  }
-  // Next unit of this CTA: tile (tm, tn), segment/split index seg, k-blocks [kb0, kb1).
-  __device__ bool next(Cursor& c, int& tm, int& tn, int& seg, int& kb0, int& kb1) const {
+  // Work unit u of this CTA: tile (tm, tn), split/segment index seg and
+  // k-blocks [kb0, kb1); false past the last unit. Static mode: tiles
+  // blockIdx.x + u*gridDim.x. Stream-K: the tiles that this CTA's k-block
+  // range [blockIdx.x*sk_per, +sk_per) touches, in order. The kernel lists the
+  // first MAX_LISTED units in shared memory once, in parallel (warp 3, while
+  // TMEM is allocated), because computing one costs a single thread about 600
+  // cycles, which every role would otherwise pay between consecutive tiles.
+  static constexpr int MAX_LISTED = 64;
+  __device__ bool unit(int u, int& tm, int& tn, int& seg, int& kb0, int& kb1) const {
     if (streamk) {
-      if (c.pos >= c.end) return false;
-      const int tile = (int)(c.pos / kblocks);
-      kb0 = (int)(c.pos % kblocks);
-      kb1 = (int)min((long long)kblocks, kb0 + (c.end - c.pos));
+      const int p0 = blockIdx.x * sk_per;
+      const int p1 = min(p0 + sk_per, tiles_m * tiles_n * kblocks);
+      if (p0 >= p1) return false;
+      const int tile = fd_kblocks.div(p0) + u;
+      const int t0 = tile * kblocks;
+      if (t0 >= p1) return false;
+      kb0 = max(p0 - t0, 0);
+      kb1 = min(p1 - t0, kblocks);
       int dummy;
       get(tile, tm, tn, dummy);
-      seg = blockIdx.x - (int)(((long long)tile * kblocks) / sk_per);
-      c.pos += kb1 - kb0;
+      seg = blockIdx.x - fd_skper.div(t0);
       return true;
     }
-    if (c.t >= total()) return false;
-    get(c.t, tm, tn, seg);
+    const int t = blockIdx.x + u * gridDim.x;
+    if (t >= total()) return false;
+    get(t, tm, tn, seg);
     krange(seg, kb0, kb1);
-    c.t += gridDim.x;
     return true;
   }
+
 };
 
 // 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
@@ -129,7 +166,23 @@ struct EpiCtx {
   int n0;
   int ks;
   bool row_ok;
+  uint64_t* tempty;  // accumulator-free barrier (for epilogues that release early)
 };
+
+// An epilogue functor with `static constexpr bool kEarlyRelease = true` hands
+// the accumulator back itself, as soon as its last tcgen05.ld has completed
+// (release_acc below) and before its global stores, so the next tile's MMAs
+// are not held up by them; the kernel then does not arrive for it.
+template <class E, class = void>
+struct EarlyRelease : std::false_type {};
+template <class E>
+struct EarlyRelease<E, std::void_t<decltype(E::kEarlyRelease)>>
+    : std::integral_constant<bool, E::kEarlyRelease> {};
+
+__device__ __forceinline__ void release_acc(const EpiCtx& c) {
+  mbd::tc_fence_before();
+  mbd::mbar_arrive(c.tempty);
+}
 
 
 // ---------------------------------------------------------------------------
@@ -201,8 +254,10 @@ struct GemmProducer {
     return mbd::sw128_desc(sB + kk * step, B_BOX_BYTES, 1024);
   }
   __device__ void load_resident(uint8_t*, uint64_t*) const {}
-  // All MMAs of one stage into accumulator d; `first` starts a fresh sum.
-  __device__ void issue(uint32_t d, uint32_t st, uint32_t /*res*/, int /*kb*/, bool first) const {
+  // All MMAs of one stage (k-block kb of output tile row tm) into accumulator
+  // d; `first` starts a fresh sum.
+  __device__ void issue(uint32_t d, uint32_t st, uint32_t /*res*/, int /*tm*/, int /*kb*/,
+                        bool first) const {
     constexpr uint32_t fmt = MODE == Mode::BF16 ? 1u : 2u;
     constexpr uint32_t idesc = mbd::make_idesc(fmt, BM, BN, 0, B_MN ? 1u : 0u);
     const uint32_t a0 = st, b0 = st + BM * KBYTES;
@@ -253,7 +308,7 @@ struct DecodeProducer {
     else
       mbd::tma_load_2d(st + AROWS * KBYTES, &b, bar, kb * KE, tn * BN);
   }
-  __device__ void issue(uint32_t d, uint32_t st, uint32_t, int, bool first) const {
+  __device__ void issue(uint32_t d, uint32_t st, uint32_t, int, int, bool first) const {
     constexpr uint32_t idesc = mbd::make_idesc(1u, BM, BN, 0, 0);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
@@ -273,7 +328,7 @@ struct DecodeProducer {
 template <int BN, int STAGES, class Producer, class Epi, int PROMOTE = 0>
 __global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ Producer prod, const __grid_constant__ Epi epi,
-                const Sched sched, uint32_t* status) {
+                const Sched sched_in, uint32_t* status) {
   using S = Smem<Producer, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -288,8 +343,11 @@ __global__ void __launch_bounds__(256, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* drain = reinterpret_cast<uint64_t*>(tmem_slot + 2);
+  int4* work = reinterpret_cast<int4*>(base + S::WORK_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Sched sched = sched_in;
+  sched.init_fast();
   auto sA = [&](int s) { return ring + s * S::STAGE_BYTES; };
 
   if (threadIdx.x == 0) {
@@ -308,99 +366,134 @@ __global__ void __launch_bounds__(256, 1)
   }
   if (warp == 0 && lane == 0) prod.prefetch();
   if (warp == 2) mbd::tmem_alloc(tmem_slot, S::TMEM_COLS);
+  if (warp == 3) {
+    for (int u = lane; u < Sched::MAX_LISTED; u += 32) {
+      int tm, tn, sg, k0, k1;
+      work[u] = sched.unit(u, tm, tn, sg, k0, k1) ? make_int4(tm, tn, sg, k0 | (k1 << 16))
+                                                  : make_int4(-1, 0, 0, 0);
+    }
+  }
+  // unit u of this CTA: from the list, or computed past its end
+  auto unit = [&](int u, int& tm, int& tn, int& sg, int& k0, int& k1) -> bool {
+    if (u < Sched::MAX_LISTED) {
+      const int4 w = work[u];
+      if (w.x < 0) return false;
+      tm = w.x;
+      tn = w.y;
+      sg = w.z;
+      k0 = w.w & 0xFFFF;
+      k1 = w.w >> 16;
+      return true;
+    }
+    return sched.unit(u, tm, tn, sg, k0, k1);
+  };
   __syncthreads();
   mbd::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // The producer and MMA warps run their loops with all 32 lanes (waits on
+  // every lane, agreed by a warp vote) and only lane 0 issues the TMA copies,
+  // MMAs and commits: a warp whose lanes 1-31 sat at the final barrier while
+  // lane 0 looped measurably slowed lane 0 down (hundreds of cycles per tile).
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued = 0;  // bit s: parity of the last load issued into stage s
-      uint32_t used = 0;    // bit s: stage s received at least one load
-      bool ok = true;
-      if constexpr (Producer::RESIDENT_BYTES > 0) {
+    // ---------------- TMA producer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0;  // bit s: parity of the last load issued into stage s
+    uint32_t used = 0;    // bit s: stage s received at least one load
+    bool ok = true;
+    if constexpr (Producer::RESIDENT_BYTES > 0) {
+      if (lane == 0) {
         mbd::mbar_expect_tx(res_full, prod.resident_tx_bytes());
         prod.load_resident(res, res_full);
       }
-      auto cur = sched.begin();
-      int tm, tn, ks, kb0, kb1;
-      while (ok && sched.next(cur, tm, tn, ks, kb0, kb1)) {
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbd::mbar_wait(&empty[stage], phase ^ 1, status, MB_DEV_TIMEOUT_TMA, abort_flag)) {
+      __syncwarp();
+    }
+    int tm, tn, ks, kb0, kb1;
+    for (int u = 0; ok && unit(u, tm, tn, ks, kb0, kb1); ++u) {
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const bool got =
+            mbd::mbar_wait(&empty[stage], phase ^ 1, status, MB_DEV_TIMEOUT_TMA, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbd::mbar_expect_tx(&full[stage], prod.stage_tx_bytes());
+          prod.load(sA(stage), &full[stage], tm, tn, kb);
+        }
+        __syncwarp();
+        issued = (issued & ~(1u << stage)) | (phase << stage);
+        used |= 1u << stage;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    // Never leave a bulk copy in flight into shared memory we are about to
+    // release: wait (bounded) for the last load of every stage.
+    for (int s = 0; s < STAGES; ++s)
+      if (used & (1u << s)) mbd::mbar_wait(&full[s], (issued >> s) & 1, status, MB_DEV_TIMEOUT_TMA);
+    if constexpr (Producer::RESIDENT_BYTES > 0) mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_TMA);
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    if constexpr (Producer::RESIDENT_BYTES > 0)
+      ok = __all_sync(0xffffffffu, mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_MMA, abort_flag));
+    const uint32_t res_u32 = mbd::smem_u32(res);
+    int i = 0;
+    int tm, tn, ks, kb0, kb1;
+    for (int u = 0; ok && unit(u, tm, tn, ks, kb0, kb1); ++u) {
+      const int nch = PROMOTE > 0 ? (kb1 - kb0 + PROMOTE - 1) / PROMOTE : 1;
+      for (int ch = 0; ok && ch < nch; ++ch, ++i) {
+        const int ka = PROMOTE > 0 ? kb0 + ch * PROMOTE : kb0;
+        const int kz = PROMOTE > 0 ? min(kb1, ka + PROMOTE) : kb1;
+        const int buf = i & 1;
+        const uint32_t tph = (i >> 1) & 1;
+        const bool got =
+            mbd::mbar_wait(&tempty[buf], tph ^ 1, status, MB_DEV_TIMEOUT_MMA, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        mbd::tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = ka; kb < kz; ++kb) {
+          const bool landed =
+              mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag);
+          if (!__all_sync(0xffffffffu, landed)) {
             ok = false;
             break;
           }
-          mbd::mbar_expect_tx(&full[stage], prod.stage_tx_bytes());
-          prod.load(sA(stage), &full[stage], tm, tn, kb);
-          issued = (issued & ~(1u << stage)) | (phase << stage);
-          used |= 1u << stage;
+          mbd::tc_fence_after();
+          if (lane == 0) {
+            prod.issue(d, mbd::smem_u32(sA(stage)), res_u32, tm, kb, kb == ka);
+            mbd::mma_commit(&empty[stage]);
+          }
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
+        if (ok && lane == 0) mbd::mma_commit(&tfull[buf]);
+        __syncwarp();
       }
-      // Never leave a bulk copy in flight into shared memory we are about to
-      // release: wait (bounded) for the last load of every stage.
-      for (int s = 0; s < STAGES; ++s)
-        if (used & (1u << s)) mbd::mbar_wait(&full[s], (issued >> s) & 1, status, MB_DEV_TIMEOUT_TMA);
-      if constexpr (Producer::RESIDENT_BYTES > 0) mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_TMA);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      if constexpr (Producer::RESIDENT_BYTES > 0)
-        ok = mbd::mbar_wait(res_full, 0, status, MB_DEV_TIMEOUT_MMA, abort_flag);
-      const uint32_t res_u32 = mbd::smem_u32(res);
-      int i = 0;
-      auto cur = sched.begin();
-      int tm, tn, ks, kb0, kb1;
-      while (ok && sched.next(cur, tm, tn, ks, kb0, kb1)) {
-        const int nch = PROMOTE > 0 ? (kb1 - kb0 + PROMOTE - 1) / PROMOTE : 1;
-        for (int ch = 0; ok && ch < nch; ++ch, ++i) {
-          const int ka = PROMOTE > 0 ? kb0 + ch * PROMOTE : kb0;
-          const int kz = PROMOTE > 0 ? min(kb1, ka + PROMOTE) : kb1;
-          const int buf = i & 1;
-          const uint32_t tph = (i >> 1) & 1;
-          if (!mbd::mbar_wait(&tempty[buf], tph ^ 1, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbd::tc_fence_after();
-          const uint32_t d = tmem + buf * BN;
-          for (int kb = ka; kb < kz; ++kb) {
-            if (!mbd::mbar_wait(&full[stage], phase, status, MB_DEV_TIMEOUT_MMA, abort_flag)) {
-              ok = false;
-              break;
-            }
-            mbd::tc_fence_after();
-            prod.issue(d, mbd::smem_u32(sA(stage)), res_u32, kb, kb == ka);
-            mbd::mma_commit(&empty[stage]);
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1;
-            }
-          }
-          if (ok) mbd::mma_commit(&tfull[buf]);
-        }
-      }
-      // All MMAs issued by this thread are complete before TMEM is freed.
-      mbd::mma_commit(drain);
-      mbd::mbar_wait(drain, 0, status, MB_DEV_TIMEOUT_MMA);
-    }
+    // All MMAs issued by lane 0 are complete before TMEM is freed.
+    if (lane == 0) mbd::mma_commit(drain);
+    __syncwarp();
+    mbd::mbar_wait(drain, 0, status, MB_DEV_TIMEOUT_MMA);
   } else if (warp >= 4 && warp < 8) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;
     int i = 0;
-    auto cur = sched.begin();
     int tm, tn, ks, kb0, kb1;
     bool ok = true;
-    while (ok && sched.next(cur, tm, tn, ks, kb0, kb1)) {
+    for (int u = 0; ok && unit(u, tm, tn, ks, kb0, kb1); ++u) {
       EpiCtx c;
       c.row = tm * BM + q * 32 + lane;
       c.n0 = tn * BN;
@@ -442,9 +535,12 @@ __global__ void __launch_bounds__(256, 1)
         if (!mbd::vote_all(got, 2, 128)) break;
         mbd::tc_fence_after();
         c.taddr = tmem + buf * BN + ((uint32_t)(q * 32) << 16);
+        c.tempty = &tempty[buf];
         epi(c);
-        mbd::tc_fence_before();
-        mbd::mbar_arrive(&tempty[buf]);
+        if constexpr (!EarlyRelease<Epi>::value) {
+          mbd::tc_fence_before();
+          mbd::mbar_arrive(&tempty[buf]);
+        }
         ++i;
       }
     }

@@ -21,6 +21,9 @@ def _bf16(torch, x):
     ((2, 9, 9, 64), (48, 1, 1, 64), 0),        # 1x1, Cout not a multiple of 32
     ((1, 12, 11, 64), (32, 5, 5, 64), 2),      # 5x5
     ((0, 8, 8, 64), (64, 3, 3, 64), 1),        # empty batch
+    ((3, 17, 23, 64), (32, 3, 3, 64), 1),      # resident path, 25-slot position rows
+    ((2, 30, 62, 64), (64, 3, 3, 64), 1),      # resident path, 64-slot rows (the widest)
+    ((2, 4, 1, 64), (64, 3, 1, 64), 0),        # resident path, 1-slot rows, 3x1 filter
 ])
 def test_conv2d_bf16(xs, ws, pad):
     import torch
