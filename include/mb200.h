@@ -263,6 +263,23 @@ size_t mb_sdpa_workspace_bytes(int64_t S);
 int mb_sdpa_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int64_t S,
                  int64_t d, void* workspace, size_t workspace_bytes, void* stream);
 
+/* out[S, D] = GQA attention of x [S, D] (llama_attention.py:22-63): qkv =
+ * x @ W_qkv (W_qkv (in, out) = [D, D + 2*Hkv*128]), per-head interleaved
+ * RoPE on q and k at positions 0..S-1 with omega_i = base^(-2i/128), softmax
+ * attention over all S keys (non-causal, H query heads sharing Hkv kv heads),
+ * then @ W_o [D, D]. Head dim 128 (D = 128*H). */
+size_t mb_llama_attention_workspace_bytes(int64_t S, int64_t D, int64_t H, int64_t Hkv);
+int mb_llama_attention_bf16(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* w_o,
+                            uint16_t* out, int64_t S, int64_t D, int64_t H, int64_t Hkv, float base,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* C[b] = A[b] @ B[b] for b < batch, fp32 row-major contiguous batches
+ * (mlx/kernels/common/batch_mm.py:10-11, registry.py:61-77, 131), 3xTF32 like
+ * mb_sqr_mm_f32. Workspace: mb_batch_mm_f32_workspace_bytes, 256-byte aligned. */
+size_t mb_batch_mm_f32_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
+int mb_batch_mm_f32(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t N,
+                    int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
 /* sqr_mm for callers that cannot allocate device memory. This entry point
  * has no counterpart in the reference. It computes exactly what
  * mb_sqr_mm_f32 computes, but takes its scratch from a 64 MiB array compiled

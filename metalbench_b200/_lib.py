@@ -74,6 +74,11 @@ SIGNATURES = {
     "mb_gemm_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "mb_sqr_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64]),
     "mb_sqr_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, C.c_size_t, _P]),
+    "mb_llama_attention_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64, _I64]),
+    "mb_llama_attention_bf16": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, _P,
+                                           C.c_size_t, _P]),
+    "mb_batch_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64, _I64]),
+    "mb_batch_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, C.c_size_t, _P]),
     "mb_conv2d_nhwc_bf16": (C.c_int, [_P, _P, _P] + [_I] * 9 + [_P]),
     "mb_attention_decode_workspace_bytes": (C.c_size_t, [_I, _I, _I, _I]),
     "mb_attention_decode_bf16": (C.c_int, [_P, _I, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _I,

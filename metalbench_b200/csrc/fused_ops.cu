@@ -104,6 +104,39 @@ __global__ void sdpa_tables_kernel(int* bt, int pages, int* start_pos, int* kv_l
   }
 }
 
+// llama_attention step 2: per-head interleaved-pair RoPE (omega_i =
+// base^(-2i/Dh), positions 0..S-1) on q in place inside qkv [S, ld], and on k
+// into the paged cache layout [S/64 pages][Hkv][64][Dh] of the attention
+// kernels, together with v (copied). One thread per (s, head, pair); heads
+// 0..H-1 are q, H..H+Hkv-1 k, H+Hkv.. v.
+__global__ void attn_rope_scatter_kernel(uint16_t* __restrict__ qkv, int64_t ld, int S, int H,
+                                         int Hkv, float neg_log2_base_over_half,
+                                         uint16_t* __restrict__ kc, uint16_t* __restrict__ vc) {
+  constexpr int Dh = 128, half = Dh / 2;
+  const int heads = H + 2 * Hkv;
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (t >= (int64_t)S * heads * half) return;
+  const int i = (int)(t % half);
+  const int hd = (int)((t / half) % heads);
+  const int s = (int)(t / ((int64_t)half * heads));
+  uint16_t* src = qkv + (int64_t)s * ld + (int64_t)hd * Dh + 2 * i;
+  uint32_t w = *reinterpret_cast<const uint32_t*>(src);
+  if (hd < H + Hkv) {
+    const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xFFFF0000u);
+    float sn, cs;
+    sincosf((float)s * exp2f(neg_log2_base_over_half * (float)i), &sn, &cs);
+    w = gemm::pack_bf16(a * cs - b * sn, a * sn + b * cs);
+  }
+  if (hd < H) {
+    *reinterpret_cast<uint32_t*>(src) = w;
+    return;
+  }
+  const int kh = hd < H + Hkv ? hd - H : hd - H - Hkv;
+  uint16_t* dst = (hd < H + Hkv ? kc : vc) +
+                  (((int64_t)(s / 64) * Hkv + kh) * 64 + (s % 64)) * Dh + 2 * i;
+  *reinterpret_cast<uint32_t*>(dst) = w;
+}
+
 }  // namespace
 
 extern "C" size_t mb_rms_norm_linear_workspace_bytes(int64_t M) {
@@ -207,4 +240,68 @@ extern "C" int mb_sdpa_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t
   // [S, 128] rows are pages of 64 keys for one kv head: an identity page table
   return mb_attention_prefill_bf16(Q, 128, K, V, bt, pages, sp, kl, 1, (int)S, 1, 1, 128, 0, O,
                                    128, stream);
+}
+
+// ---- llama_attention (mlx/kernels/standard/llama_attention.py:22-63) ------
+namespace {
+struct LlamaAttnWs {
+  size_t qkv, kc, o, tables, total;
+};
+LlamaAttnWs llama_attn_ws(int64_t S, int64_t D, int64_t Hkv) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const int64_t pages = (S + 63) / 64;
+  LlamaAttnWs w;
+  w.qkv = al((size_t)S * (D + 2 * Hkv * 128) * 2);
+  w.kc = al((size_t)pages * Hkv * 64 * 128 * 2);
+  w.o = al((size_t)S * D * 2);
+  w.tables = al((size_t)(pages + 2) * 4);
+  w.total = w.qkv + 2 * w.kc + w.o + w.tables;
+  return w;
+}
+}  // namespace
+
+extern "C" size_t mb_llama_attention_workspace_bytes(int64_t S, int64_t D, int64_t H,
+                                                     int64_t Hkv) {
+  if (S <= 0 || D <= 0 || H <= 0 || Hkv <= 0) return 0;
+  return llama_attn_ws(S, D, Hkv).total;
+}
+
+extern "C" int mb_llama_attention_bf16(const uint16_t* x, const uint16_t* w_qkv,
+                                       const uint16_t* w_o, uint16_t* out, int64_t S, int64_t D,
+                                       int64_t H, int64_t Hkv, float base, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  MB_REQUIRE(S >= 0 && H > 0 && Hkv > 0 && H % Hkv == 0 && D == H * 128,
+             "llama_attention: need D = 128 * H and H a multiple of H_kv");
+  if (S == 0) return MB_OK;
+  MB_REQUIRE(S <= (1 << 24), "llama_attention: S too large");
+  const LlamaAttnWs wl = llama_attn_ws(S, D, Hkv);
+  MB_REQUIRE(workspace && workspace_bytes >= wl.total,
+             "llama_attention: workspace of %zu bytes required", wl.total);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  uint16_t* qkv = reinterpret_cast<uint16_t*>(w);
+  uint16_t* kc = reinterpret_cast<uint16_t*>(w + wl.qkv);
+  uint16_t* vc = reinterpret_cast<uint16_t*>(w + wl.qkv + wl.kc);
+  uint16_t* o = reinterpret_cast<uint16_t*>(w + wl.qkv + 2 * wl.kc);
+  int* bt = reinterpret_cast<int*>(w + wl.qkv + 2 * wl.kc + wl.o);
+  const int pages = (int)((S + 63) / 64);
+  int* sp = bt + pages;
+  int* kl = sp + 1;
+  const int64_t nqkv = D + 2 * Hkv * 128;
+  // 1. qkv = x @ W_qkv (W in the reference's (in, out) layout)
+  int rc = mb_gemm_bf16(x, w_qkv, qkv, S, nqkv, D, 1, stream);
+  if (rc) return rc;
+  // 2. RoPE on q (in place) and k, K/V into pages; identity page table
+  const int64_t n = S * (H + 2 * Hkv) * 64;
+  attn_rope_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+      qkv, nqkv, (int)S, (int)H, (int)Hkv, -log2f(base) / 64.f, kc, vc);
+  MB_CUDA(cudaGetLastError());
+  sdpa_tables_kernel<<<1, 256, 0, s>>>(bt, pages, sp, kl, (int)S);
+  MB_CUDA(cudaGetLastError());
+  // 3. non-causal GQA attention over all S keys
+  rc = mb_attention_prefill_bf16(qkv, (int)nqkv, kc, vc, bt, pages, sp, kl, 1, (int)S, (int)H,
+                                 (int)Hkv, 128, 0, o, (int)D, stream);
+  if (rc) return rc;
+  // 4. out = o @ W_o
+  return mb_gemm_bf16(o, w_o, out, S, D, D, 1, stream);
 }

@@ -61,10 +61,14 @@ __global__ void split_a_kernel(const float4* __restrict__ a, float4* __restrict_
 }
 
 // B [K,N] -> Bt_hi, Bt_lo [N,K] (transposed so both GEMM operands are K-major),
-// 32x32 tiles through a padded shared tile.
+// 32x32 tiles through a padded shared tile; blockIdx.z = batch (strides K*N).
 __global__ void split_bt_kernel(const float* __restrict__ b, float* __restrict__ hi,
                                 float* __restrict__ lo, int64_t K, int64_t N) {
   __shared__ float T[32][33];
+  const int64_t z = blockIdx.z;
+  b += z * K * N;
+  hi += z * K * N;
+  lo += z * K * N;
   const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
   for (int r = ty; r < 32; r += 8)
@@ -81,75 +85,131 @@ __global__ void split_bt_kernel(const float* __restrict__ b, float* __restrict__
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-}  // namespace
-
-extern "C" size_t mb_sqr_mm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
-  return 2 * align256((size_t)M * K * 4) + 2 * align256((size_t)N * K * 4);
+size_t tf32x3_workspace(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  return 2 * align256((size_t)batch * M * K * 4) + 2 * align256((size_t)batch * N * K * 4);
 }
 
-extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
-                             int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
-  MB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "mb_sqr_mm_f32: negative dimension");
-  if (M == 0 || N == 0) return MB_OK;
-  MB_REQUIRE(K > 0, "mb_sqr_mm_f32: K must be positive");
-  MB_REQUIRE(K % 4 == 0, "mb_sqr_mm_f32: K must be a multiple of 4");
-  MB_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0, "mb_sqr_mm_f32: A must be 16-byte aligned");
-  const size_t need = mb_sqr_mm_f32_workspace_bytes(M, N, K);
-  MB_REQUIRE(workspace != nullptr && workspace_bytes >= need &&
-                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
-             "mb_sqr_mm_f32: workspace of %zu bytes (256-byte aligned) required, got %zu", need,
-             workspace_bytes);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
+// C[b] = A[b] @ B[b] for b < batch (row-major, contiguous batches) with
+// 3xTF32: split prepass into the workspace, then one persistent GEMM launch
+// whose tile rows run over all batches. M % 128 == 0 when batch > 1, so no
+// 128-row tile straddles two batches; B rows of batch b start at b*N in the
+// transposed operand (GemmProducer::b_rows_per_batch).
+int tf32x3_gemm(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t N,
+                int64_t K, uint8_t* w, uint32_t* status, cudaStream_t s) {
   float* a_hi = reinterpret_cast<float*>(w);
-  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)M * K * 4));
-  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4));
-  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4) +
-                                         align256((size_t)N * K * 4));
-  const int64_t n4 = M * K / 4;
+  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)batch * M * K * 4));
+  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)batch * M * K * 4));
+  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)batch * M * K * 4) +
+                                         align256((size_t)batch * N * K * 4));
   const int sms = mb::num_sms();
   split_a_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(A),
                                           reinterpret_cast<float4*>(a_hi),
-                                          reinterpret_cast<float4*>(a_lo), n4);
+                                          reinterpret_cast<float4*>(a_lo), batch * M * K / 4);
   MB_CUDA(cudaGetLastError());
-  dim3 g((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
-  MB_REQUIRE(g.y <= 65535, "mb_sqr_mm_f32: K too large");
+  dim3 g((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32), (unsigned)batch);
+  MB_REQUIRE(g.y <= 65535 && g.z <= 65535, "tf32x3: K or batch too large");
   split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
   MB_CUDA(cudaGetLastError());
 
   using P = GemmProducer<Mode::TF32X3, 128, false>;
   using S = Smem<P, 128, 3>;
   gemm::Epi<128, gemm::EpiStore> e{};
-  e.M = (int)M;
+  e.M = (int)(batch * M);
   e.N = (int)N;
   e.out = C;
   e.ldo = N;
   e.out_f32 = 1;
   e.alpha = 1.f;
   P p;
+  if (batch > 1) {
+    p.a_tiles_per_batch = (int)(M / BM);
+    p.b_rows_per_batch = (int)N;
+  }
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  int rc = mb::make_tmap_2d(&p.a, a_hi, dt, 4, K, M, K * 4, P::KE, BM, sw);
-  if (!rc) rc = mb::make_tmap_2d(&p.alo, a_lo, dt, 4, K, M, K * 4, P::KE, BM, sw);
-  if (!rc) rc = mb::make_tmap_2d(&p.b, b_hi, dt, 4, K, N, K * 4, P::KE, 128, sw);
-  if (!rc) rc = mb::make_tmap_2d(&p.blo, b_lo, dt, 4, K, N, K * 4, P::KE, 128, sw);
+  const int64_t rows_a = batch * M, rows_b = batch * N;
+  int rc = mb::make_tmap_2d(&p.a, a_hi, dt, 4, K, rows_a, K * 4, P::KE, BM, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.alo, a_lo, dt, 4, K, rows_a, K * 4, P::KE, BM, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.b, b_hi, dt, 4, K, rows_b, K * 4, P::KE, 128, sw);
+  if (!rc) rc = mb::make_tmap_2d(&p.blo, b_lo, dt, 4, K, rows_b, K * 4, P::KE, 128, sw);
   if (rc) return rc;
   Sched sc;
-  sc.tiles_m = (int)((M + BM - 1) / BM);
+  sc.tiles_m = (int)((batch * M + BM - 1) / BM);
   sc.tiles_n = (int)((N + 127) / 128);
   sc.kblocks = (int)((K + P::KE - 1) / P::KE);
   sc.ksplit = 1;
   sc.kb_per_split = sc.kblocks;
   auto kern = gemm_kernel<128, 3, P, decltype(e), kTf32PromoteBlocks>;
-  static bool attr = false;
-  if (!attr) {
+  int dev = 0;
+  MB_CUDA(cudaGetDevice(&dev));
+  static bool attr[64] = {};  // the attribute is set per device
+  if (dev < 0 || dev >= 64 || !attr[dev]) {
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-    attr = true;
+    if (dev >= 0 && dev < 64) attr[dev] = true;
   }
   const int grid = sc.total() < sms ? sc.total() : sms;
-  kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, mb::device_status_ptr());
+  kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, status);
   MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+int check_tf32x3_args(const char* fn, const float* A, int64_t batch, int64_t M, int64_t N,
+                      int64_t K) {
+  MB_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "%s: negative dimension", fn);
+  if (batch == 0 || M == 0 || N == 0) return MB_OK;
+  MB_REQUIRE(K > 0, "%s: K must be positive", fn);
+  MB_REQUIRE(K % 4 == 0, "%s: K must be a multiple of 4", fn);
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0, "%s: A must be 16-byte aligned", fn);
+  return MB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t mb_sqr_mm_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return tf32x3_workspace(1, M, N, K);
+}
+
+extern "C" int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                             int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_tf32x3_args("mb_sqr_mm_f32", A, 1, M, N, K);
+  if (rc || M == 0 || N == 0) return rc;
+  const size_t need = mb_sqr_mm_f32_workspace_bytes(M, N, K);
+  MB_REQUIRE(workspace != nullptr && workspace_bytes >= need &&
+                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "mb_sqr_mm_f32: workspace of %zu bytes (256-byte aligned) required, got %zu", need,
+             workspace_bytes);
+  return tf32x3_gemm(A, B, C, 1, M, N, K, static_cast<uint8_t*>(workspace),
+                     mb::device_status_ptr(), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mb_batch_mm_f32_workspace_bytes(int64_t batch, int64_t M, int64_t N,
+                                                  int64_t K) {
+  if (batch <= 0 || M <= 0 || N <= 0 || K <= 0) return 0;
+  // one launch over all batches when M is a whole number of 128-row tiles,
+  // else batch-by-batch through one batch's workspace
+  return M % BM == 0 ? tf32x3_workspace(batch, M, N, K) : tf32x3_workspace(1, M, N, K);
+}
+
+extern "C" int mb_batch_mm_f32(const float* A, const float* B, float* C, int64_t batch, int64_t M,
+                               int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  int rc = check_tf32x3_args("mb_batch_mm_f32", A, batch, M, N, K);
+  if (rc || batch == 0 || M == 0 || N == 0) return rc;
+  const size_t need = mb_batch_mm_f32_workspace_bytes(batch, M, N, K);
+  MB_REQUIRE(workspace != nullptr && workspace_bytes >= need &&
+                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "mb_batch_mm_f32: workspace of %zu bytes (256-byte aligned) required, got %zu", need,
+             workspace_bytes);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M % BM == 0) return tf32x3_gemm(A, B, C, batch, M, N, K, w, mb::device_status_ptr(), s);
+  MB_REQUIRE(((M * K) % 4) == 0, "mb_batch_mm_f32: M*K must be a multiple of 4");
+  for (int64_t b = 0; b < batch; ++b) {
+    rc = tf32x3_gemm(A + b * M * K, B + b * K * N, C + b * M * N, 1, M, N, K, w,
+                     mb::device_status_ptr(), s);
+    if (rc) return rc;
+  }
   return MB_OK;
 }
 
@@ -219,50 +279,6 @@ extern "C" int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, i
 
   // The split prepass overwrites every scratch byte the GEMM reads, so nothing
   // has to be cleared first.
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* w = static_cast<uint8_t*>(slot->scratch);
-  float* a_hi = reinterpret_cast<float*>(w);
-  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)M * K * 4));
-  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4));
-  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)M * K * 4) +
-                                         align256((size_t)N * K * 4));
-  const int sms = mb::num_sms();
-  split_a_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(A),
-                                          reinterpret_cast<float4*>(a_hi),
-                                          reinterpret_cast<float4*>(a_lo), M * K / 4);
-  MB_CUDA(cudaGetLastError());
-  dim3 g((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
-  MB_REQUIRE(g.y <= 65535, "mb_sqr_mm_f32_noalloc: K too large");
-  split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
-  MB_CUDA(cudaGetLastError());
-
-  using P = GemmProducer<Mode::TF32X3, 128, false>;
-  using S = Smem<P, 128, 3>;
-  gemm::Epi<128, gemm::EpiStore> e{};
-  e.M = (int)M;
-  e.N = (int)N;
-  e.out = C;
-  e.ldo = N;
-  e.out_f32 = 1;
-  e.alpha = 1.f;
-  P p;
-  const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  rc = mb::make_tmap_2d(&p.a, a_hi, dt, 4, K, M, K * 4, P::KE, BM, sw);
-  if (!rc) rc = mb::make_tmap_2d(&p.alo, a_lo, dt, 4, K, M, K * 4, P::KE, BM, sw);
-  if (!rc) rc = mb::make_tmap_2d(&p.b, b_hi, dt, 4, K, N, K * 4, P::KE, 128, sw);
-  if (!rc) rc = mb::make_tmap_2d(&p.blo, b_lo, dt, 4, K, N, K * 4, P::KE, 128, sw);
-  if (rc) return rc;
-  Sched sc;
-  sc.tiles_m = (int)((M + BM - 1) / BM);
-  sc.tiles_n = (int)((N + 127) / 128);
-  sc.kblocks = (int)((K + P::KE - 1) / P::KE);
-  sc.ksplit = 1;
-  sc.kb_per_split = sc.kblocks;
-  auto kern = gemm_kernel<128, 3, P, decltype(e), kTf32PromoteBlocks>;
-  MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-  const int grid = sc.total() < sms ? sc.total() : sms;
-  kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, slot->status);
-  MB_CUDA(cudaGetLastError());
-  return MB_OK;
+  return tf32x3_gemm(A, B, C, 1, M, N, K, static_cast<uint8_t*>(slot->scratch), slot->status,
+                     static_cast<cudaStream_t>(stream));
 }

@@ -205,6 +205,13 @@ struct GemmProducer {
   // shared-memory image, fetched with one bulk copy instead of a TMA box.
   const uint8_t* b_tiled = nullptr;
   int b_kblocks = 0;
+  // Batched K-major B (TF32x3 batch_mm): tile row tm belongs to batch
+  // tm / a_tiles_per_batch, whose B rows start at batch * b_rows_per_batch.
+  int a_tiles_per_batch = 0;
+  int b_rows_per_batch = 0;
+  __device__ int b_row(int tm, int tn) const {
+    return (a_tiles_per_batch ? tm / a_tiles_per_batch * b_rows_per_batch : 0) + tn * BN;
+  }
   static constexpr int KE = KBYTES / elem_bytes(MODE);  // K elements per stage
   static constexpr int PARTS = MODE == Mode::TF32X3 ? 2 : 1;
   static constexpr uint32_t BYTES = PARTS * (BM + BN) * KBYTES;
@@ -231,7 +238,7 @@ struct GemmProducer {
         mbd::bulk_load(sB, b_tiled + ((size_t)tn * b_kblocks + kb) * (BN * KBYTES), BN * KBYTES,
                        bar);
       else
-        mbd::tma_load_2d(sB, &b, bar, kb * KE, tn * BN);
+        mbd::tma_load_2d(sB, &b, bar, kb * KE, b_row(tm, tn));
     } else {
 #pragma unroll
       for (int j = 0; j < BN / KE; ++j)
@@ -239,7 +246,7 @@ struct GemmProducer {
     }
     if constexpr (MODE == Mode::TF32X3) {
       mbd::tma_load_2d(sB + BN * KBYTES, &alo, bar, kb * KE, tm * BM);
-      mbd::tma_load_2d(sB + BN * KBYTES + BM * KBYTES, &blo, bar, kb * KE, tn * BN);
+      mbd::tma_load_2d(sB + BN * KBYTES + BM * KBYTES, &blo, bar, kb * KE, b_row(tm, tn));
     }
   }
   // Shared-memory descriptors for MMA k-step kk of a stage.

@@ -114,6 +114,41 @@ int prep_sqr_mm(const RunArgs& a, KernelState& st, cudaStream_t) {
   return MB_OK;
 }
 
+// batch_mm: registry batched_matmul helper common/registry.py:61-77 — A@0
+// [batch, M, K], B@1 [batch, K, N], C@2 [batch, M, N], M@3, N@4, K@5 (the batch
+// count follows from A's size), fp32.
+int prep_batch_mm(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *A, *B, *Cb;
+  int64_t M, N, K;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &A));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &B));
+  TRY(need_buf(a, 2, MB_ROLE_OUTPUT, &Cb));
+  TRY(need_scalar(a, 3, &M));
+  TRY(need_scalar(a, 4, &N));
+  TRY(need_scalar(a, 5, &K));
+  MB_REQUIRE(M > 0 && K > 0 && A->bytes % (size_t)(M * K * 4) == 0, "batch_mm: A size");
+  const int64_t batch = (int64_t)(A->bytes / (size_t)(M * K * 4));
+  MB_REQUIRE(B->bytes == (size_t)(batch * K * N * 4) && Cb->bytes == (size_t)(batch * M * N * 4),
+             "batch_mm: buffer sizes do not match batch=%lld M=%lld N=%lld K=%lld",
+             (long long)batch, (long long)M, (long long)N, (long long)K);
+  const void *pa = A->dev, *pb = B->dev;
+  void* pc = Cb->dev;
+  const size_t wsb = mb_batch_mm_f32_workspace_bytes(batch, M, N, K);
+  void* ws = nullptr;
+  if (wsb) {
+    MB_CUDA(cudaMalloc(&ws, wsb));
+    st.scratch.push_back(ws);
+  }
+  st.threads_per_cta = 256;
+  st.smem_bytes = 197752;
+  st.launches_per_iter = 3;
+  st.launch = [=](cudaStream_t s) {
+    return mb_batch_mm_f32((const float*)pa, (const float*)pb, (float*)pc, batch, M, N, K, ws,
+                           wsb, s);
+  };
+  return MB_OK;
+}
+
 // gemm_bf16: same bindings with bf16 buffers; config "b_layout" 0/1 (default 1).
 int prep_gemm_bf16(const RunArgs& a, KernelState& st, cudaStream_t) {
   const RunArgs::Buf *A, *B, *Cb;
@@ -418,6 +453,42 @@ int prep_sdpa(const RunArgs& a, KernelState& st, cudaStream_t) {
   return MB_OK;
 }
 
+// llama_attention: standard/registry.py:398-413 — x@0 [S, D], W_qkv@1
+// [D, D + 2*Hkv*Dh], W_o@2 [D, D], out@3; S@4, D@5, H@6, H_kv@7, base@8 (f32).
+int prep_llama_attention(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *wqkv, *wo, *o;
+  int64_t S, D, H, Hkv;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &wqkv));
+  TRY(need_buf(a, 2, MB_ROLE_INPUT, &wo));
+  TRY(need_buf(a, 3, MB_ROLE_OUTPUT, &o));
+  TRY(need_scalar(a, 4, &S));
+  TRY(need_scalar(a, 5, &D));
+  TRY(need_scalar(a, 6, &H));
+  TRY(need_scalar(a, 7, &Hkv));
+  double base = 10000.0;
+  a.scalar(8, &base);
+  TRY(bf16_all({x, wqkv, wo, o}, "llama_attention"));
+  MB_REQUIRE(H > 0 && D == 128 * H, "llama_attention: head dim must be 128 (D = 128*H)");
+  MB_REQUIRE(x->bytes == (size_t)(S * D * 2) && o->bytes == x->bytes &&
+                 wqkv->bytes == (size_t)(D * (D + 2 * Hkv * 128) * 2) &&
+                 wo->bytes == (size_t)(D * D * 2),
+             "llama_attention: buffer sizes do not match S/D/H_kv");
+  const size_t wsb = mb_llama_attention_workspace_bytes(S, D, H, Hkv);
+  void* ws = nullptr;
+  MB_CUDA(cudaMalloc(&ws, wsb));
+  st.scratch.push_back(ws);
+  const void *px = x->dev, *pq = wqkv->dev, *pw = wo->dev;
+  void* po = o->dev;
+  const float fb = (float)base;
+  st.launches_per_iter = 5;
+  st.launch = [=](cudaStream_t s) {
+    return mb_llama_attention_bf16((const uint16_t*)px, (const uint16_t*)pq, (const uint16_t*)pw,
+                                   (uint16_t*)po, S, D, H, Hkv, fb, ws, wsb, s);
+  };
+  return MB_OK;
+}
+
 }  // namespace
 
 void register_all_kernels() {
@@ -426,6 +497,7 @@ void register_all_kernels() {
     register_kernel({"transpose_2d", prep_transpose_2d});
     register_kernel({"transpose_batched", prep_transpose_batched});
     register_kernel({"sqr_mm", prep_sqr_mm});
+    register_kernel({"batch_mm", prep_batch_mm});
     register_kernel({"gemm_bf16", prep_gemm_bf16});
     register_kernel({"conv2d", prep_conv2d});
     register_kernel({"llama_decoder_layer", prep_llama});
@@ -434,6 +506,7 @@ void register_all_kernels() {
     register_kernel({"rope_embedding", prep_rope});
     register_kernel({"swiglu", prep_swiglu});
     register_kernel({"scaled_dot_product", prep_sdpa});
+    register_kernel({"llama_attention", prep_llama_attention});
   });
 }
 

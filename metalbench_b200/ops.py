@@ -114,6 +114,23 @@ def sqr_mm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) ->
     return out
 
 
+def batch_mm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """fp32 C[i] = A[i] @ B[i] for a [batch, M, K] and b [batch, K, N], 3xTF32."""
+    _cuda(a, "batch_mm(a)", (torch.float32,))
+    _cuda(b, "batch_mm(b)", (torch.float32,))
+    init(a.device.index)
+    Bt, M, K = a.shape
+    Bb, Kb, N = b.shape
+    if (Bb, Kb) != (Bt, K):
+        raise ValueError(f"batch_mm: shapes {tuple(a.shape)} and {tuple(b.shape)} do not match")
+    out = torch.empty((Bt, M, N), dtype=torch.float32, device=a.device)
+    ws_bytes = _lib.lib().mb_batch_mm_f32_workspace_bytes(Bt, M, N, K)
+    ws = _workspace(ws_bytes, a.device)
+    _lib.call("mb_batch_mm_f32", a.data_ptr(), b.data_ptr(), out.data_ptr(), Bt, M, N, K,
+              ws.data_ptr() if ws_bytes else None, ws_bytes, _stream())
+    return out
+
+
 _ws: dict = {}
 
 
@@ -216,3 +233,19 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     _lib.call("mb_sdpa_bf16", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), S,
               q.shape[1], ws.data_ptr(), nb, _stream())
     return o
+
+
+def llama_attention(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, n_heads: int,
+                    n_kv_heads: int, base: float = 10000.0) -> torch.Tensor:
+    """GQA self-attention with RoPE over x [S, D] (bf16, head dim 128, non-causal):
+    (softmax(rope(x Wq) rope(x Wk)^T / sqrt(128)) x Wv) @ W_o, weights (in, out)."""
+    for n, t in (("x", x), ("w_qkv", w_qkv), ("w_o", w_o)):
+        _cuda(t, f"llama_attention({n})", (torch.bfloat16,))
+    init(x.device.index)
+    S, D = x.shape
+    out = torch.empty((S, D), dtype=torch.bfloat16, device=x.device)
+    nb = _lib.lib().mb_llama_attention_workspace_bytes(S, D, n_heads, n_kv_heads)
+    ws = _workspace(nb, x.device)
+    _lib.call("mb_llama_attention_bf16", x.data_ptr(), w_qkv.data_ptr(), w_o.data_ptr(),
+              out.data_ptr(), S, D, n_heads, n_kv_heads, base, ws.data_ptr(), nb, _stream())
+    return out

@@ -82,3 +82,16 @@ REGISTRY["rect_mm"] = dict(
     rtol=1e-4, atol=1e-3, seed=0, flops=2 * 1024 * 2048 * 4096,
     bytes=4 * (1024 * 4096 + 4096 * 2048 + 1024 * 2048),
     roof="tensor_tf32x3", ref_warmup=1, ref_iters=5)
+
+# batched_matmul helper semantics (common/registry.py:61-77): A [B,M,K], B [B,K,N];
+# the reference's own shape (131): 128 x (128x256 @ 256x512)
+REGISTRY["batch_mm"] = dict(
+    kernel="batch_mm", metal_function="batch_matmul_f32",
+    input_bindings=(0, 1), input_shapes=[(128, 128, 256), (128, 256, 512)],
+    input_dtypes=["f32", "f32"], input_init=[("normal", 1.0), ("normal", 1.0)],
+    output_shape=(128, 128, 512), output_dtype="f32",
+    scalars=[dict(binding=3, dtype="u32", value=128), dict(binding=4, dtype="u32", value=512),
+             dict(binding=5, dtype="u32", value=256)],
+    rtol=1e-4, atol=1e-3, seed=0, flops=128 * 2 * 128 * 512 * 256,
+    bytes=128 * 4 * (128 * 256 + 256 * 512 + 128 * 512),
+    roof="tensor_tf32x3", ref_warmup=1, ref_iters=5)

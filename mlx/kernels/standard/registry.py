@@ -63,3 +63,21 @@ REGISTRY["scaled_dot_product"] = dict(
     scalars=[_u32(4, S_ATT), _u32(5, 128)], model_kwargs=dict(d_head=128),
     rtol=2e-2, atol=2e-2, seed=3, flops=4 * S_ATT * S_ATT * 128,
     bytes=4 * S_ATT * 128 * 2, roof="tensor_bf16", ref_warmup=1, ref_iters=3)
+
+# llama_attention (reference standard/registry.py:398-413: S 64, D 128, 4/2
+# heads of 32, fp32) at the BASELINE decoder's attention shape: S 4096,
+# d_model 4096, 32 query / 8 kv heads of 128, bf16.
+LA_S, LA_D, LA_H, LA_HKV = 4096, 4096, 32, 8
+LA_N = LA_D + 2 * LA_HKV * 128
+REGISTRY["llama_attention"] = dict(
+    kernel="llama_attention", metal_function="llama_attention_f32",
+    input_bindings=(0, 1, 2), input_shapes=[(LA_S, LA_D), (LA_D, LA_N), (LA_D, LA_D)],
+    input_dtypes=["bf16"] * 3, input_init=[("normal", 1.0), ("normal", 0.02), ("normal", 0.02)],
+    output_shape=(LA_S, LA_D), output_dtype="bf16",
+    scalars=[_u32(4, LA_S), _u32(5, LA_D), _u32(6, LA_H), _u32(7, LA_HKV),
+             dict(binding=8, dtype="f32", value=10000.0)],
+    model_kwargs=dict(S=LA_S, D=LA_D, H=LA_H, H_kv=LA_HKV, base=10000.0),
+    rtol=2e-2, atol=2e-2, seed=3,
+    flops=2 * LA_S * LA_D * LA_N + 4 * LA_H * LA_S * LA_S * 128 + 2 * LA_S * LA_D * LA_D,
+    bytes=2 * (2 * LA_S * LA_D + LA_D * LA_N + LA_D * LA_D), roof="tensor_bf16",
+    ref_warmup=0, ref_iters=1)

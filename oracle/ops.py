@@ -272,3 +272,29 @@ def sdpa(Q, K, V, acc=np.float64):
     s = s - s.max(axis=-1, keepdims=True)
     p = np.exp(s)
     return ((p / p.sum(axis=-1, keepdims=True)) @ v).astype(np.float32)
+
+
+def llama_attention(x, W_qkv, W_o, *, H: int, H_kv: int, base: float = 10000.0,
+                    acc=np.float64):
+    """Grouped-query self-attention with RoPE, no mask, no cache
+    (mlx/kernels/standard/llama_attention.py:22-63): qkv = x @ W_qkv; q/k/v
+    heads of Dh = D/H; RoPE (pairs (2i, 2i+1), positions 0..S-1) on q and k;
+    query head h uses kv head h // (H/H_kv); softmax(q k^T / sqrt(Dh)) v; @ W_o."""
+    S, D = x.shape
+    Dh = D // H
+    qkv = x.astype(acc) @ W_qkv.astype(acc)
+    q = qkv[:, :D].reshape(S, H, Dh).transpose(1, 0, 2)
+    k = qkv[:, D:D + H_kv * Dh].reshape(S, H_kv, Dh).transpose(1, 0, 2)
+    v = qkv[:, D + H_kv * Dh:].reshape(S, H_kv, Dh).transpose(1, 0, 2)
+    pos = np.arange(S)
+    q = rope(q, pos, base)
+    k = rope(k, pos, base)
+    g = H // H_kv
+    k = np.repeat(k, g, axis=0)
+    v = np.repeat(v, g, axis=0)
+    sc = q @ k.transpose(0, 2, 1) / np.sqrt(acc(Dh))
+    sc = sc - sc.max(axis=-1, keepdims=True)
+    p = np.exp(sc)
+    p = p / p.sum(axis=-1, keepdims=True)
+    o = (p @ v).transpose(1, 0, 2).reshape(S, D)
+    return (o @ W_o.astype(acc)).astype(np.float32)

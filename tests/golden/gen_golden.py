@@ -44,6 +44,8 @@ CASES = [
     ("scaled_dot_product", "standard", [(40, 128), (40, 128), (40, 128)], 5),
     ("fused_qkv_projection", "standard", [(16, 64), (64, 48)], 5),
     ("rect_mm", "common", [(32, 96), (96, 40)], 5),
+    ("batch_mm", "common", [(3, 16, 24), (3, 24, 20)], 5),
+    ("llama_attention", "standard", [(64, 128), (128, 256), (128, 128)], 5),
 ]
 
 

@@ -20,10 +20,13 @@ def _np(t):
     return O.bf16_to_f32(t.view(torch.int16).cpu().numpy().view(np.uint16))
 
 
-def _check(got, ref, tol=2e-2):
+def _check(got, ref, tol=2e-2, frac=1.0):
     atol = tol * float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)) or 1.0)
     r = O.allclose_report(got, ref, rtol=tol, atol=atol)
-    assert r["all"], r
+    if frac >= 1.0:
+        assert r["all"], r
+    else:  # the registry gate: a fraction of elements, and no element far off
+        assert r["frac_within_tol"] >= frac and r["max_err"] <= 5 * atol, r
 
 
 def _r(rng, *s, scale=1.0):
@@ -106,3 +109,20 @@ def test_fused_qkv_projection_and_rect_mm_through_gemms():
     got = ops.sqr_mm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()).cpu().numpy()
     ref = O.sqr_mm(A, B)
     assert np.abs(got - ref).max() / np.abs(ref).max() <= 1e-4
+
+
+@pytest.mark.parametrize("S,H,Hkv", [(256, 4, 2), (200, 4, 1), (1024, 8, 2), (64, 2, 2),
+                                     (2048, 8, 2)])
+def test_llama_attention(S, H, Hkv):
+    """x @ W_qkv -> RoPE -> non-causal GQA attention -> @ W_o (head dim 128).
+    Gate: >= 99.9 % of elements within the bf16 tolerance, none beyond 5x."""
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(16)
+    D = 128 * H
+    x = _r(rng, S, D)
+    wqkv = _r(rng, D, D + 2 * Hkv * 128, scale=D ** -0.5)
+    wo = _r(rng, D, D, scale=D ** -0.5)
+    got = ops.llama_attention(_bf(torch, x), _bf(torch, wqkv), _bf(torch, wo), H, Hkv)
+    # q/k/v and the attention output pass through bf16 between the four steps
+    _check(_np(got), O.llama_attention(x, wqkv, wo, H=H, H_kv=Hkv), frac=0.999)

@@ -104,3 +104,19 @@ def test_sqr_mm_f32_elementwise_gate_deep_k(M, N, K):
     ref = A.astype(np.float64) @ B.astype(np.float64)
     r = O.allclose_report(got, ref, rtol=1e-4, atol=1e-3)
     assert r["all"], r
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(128, 128, 512, 256), (3, 256, 200, 64), (5, 100, 72, 36),
+                                         (1, 128, 128, 128)])
+def test_batch_mm_f32(batch, M, N, K):
+    """batch_mm (one launch over all batches when M % 128 == 0, else batch by
+    batch) against the float64 product, fp32 gate on every element."""
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(7)
+    A = rng.standard_normal((batch, M, K)).astype(np.float32)
+    B = rng.standard_normal((batch, K, N)).astype(np.float32)
+    got = ops.batch_mm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()).cpu().numpy()
+    ref = np.matmul(A.astype(np.float64), B.astype(np.float64))
+    r = O.allclose_report(got, ref, rtol=1e-4, atol=1e-3)
+    assert r["all"], r

@@ -127,7 +127,8 @@ def test_grade_targets():
 @pytest.mark.parametrize("name,nin", [("rms_norm_linear", 2), ("fused_add_rms_norm", 2),
                                       ("rope_embedding", 1), ("swiglu", 3),
                                       ("scaled_dot_product", 3), ("fused_qkv_projection", 2),
-                                      ("rect_mm", 2), ("sqr_mm", 2), ("transpose_2d", 1)])
+                                      ("rect_mm", 2), ("batch_mm", 2), ("llama_attention", 3), ("sqr_mm", 2),
+                                      ("transpose_2d", 1)])
 def test_our_hooks_reproduce_reference_hooks(name, nin):
     """Each hook under mlx/kernels/ (default arguments) reproduces the golden
     output of the reference's own hook on the same inputs."""

@@ -110,6 +110,8 @@ def test_allclose_report_fraction():
     ("scaled_dot_product", lambda d: O.sdpa(d["in0"], d["in1"], d["in2"])),
     ("fused_qkv_projection", lambda d: O.sqr_mm(d["in0"], d["in1"])),
     ("rect_mm", lambda d: O.sqr_mm(d["in0"], d["in1"])),
+    ("batch_mm", lambda d: O.sqr_mm(d["in0"], d["in1"])),
+    ("llama_attention", lambda d: O.llama_attention(d["in0"], d["in1"], d["in2"], H=4, H_kv=2)),
 ])
 def test_standard_set_oracle_matches_reference_hooks(name, fn):
     d = _load(name)
