@@ -441,24 +441,11 @@ def print_report(result: dict, target: str, score: float) -> None:
 
 
 def update_best_times_md() -> None:
-    """Regenerate best_times.md from session.json (all chip buckets)."""
-    if not SESSION_PATH.exists():
-        return
-    session = json.loads(SESSION_PATH.read_text())
-    chips = sorted(session)
-    lines = ["# MetalBench Best Times", "",
-             "| kernel | " + " | ".join(f"{c} ms | {c} speedup | {c} SoL" for c in chips) + " |",
-             "|---|" + "---|" * (3 * len(chips))]
-    names = sorted({n for c in session.values() for n in c})
-    for n in names:
-        cols = [n]
-        for c in chips:
-            d = session[c].get(n, {})
-            cols += [f"{d['best_time_ms']:.3f}" if d.get("best_time_ms") else "--",
-                     f"{d['speedup_vs_mlx']:.1f}×" if d.get("speedup_vs_mlx") else "--",
-                     f"{d['roofline_sol'] * 100:.0f}%" if d.get("roofline_sol") else "--"]
-        lines.append("| " + " | ".join(cols) + " |")
-    (REPO_ROOT / "best_times.md").write_text("\n".join(lines) + "\n")
+    """Regenerate best_times.md and LINK.md from session.json (all chip buckets;
+    scripts/render_best_times.py and render_link_md.py in the reference)."""
+    from metalbench_b200 import leaderboard
+    leaderboard.render_best_times()
+    leaderboard.render_link_md()
 
 
 def main(argv=None) -> int:
