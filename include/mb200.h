@@ -273,6 +273,24 @@ int mb_llama_attention_bf16(const uint16_t* x, const uint16_t* w_qkv, const uint
                             uint16_t* out, int64_t S, int64_t D, int64_t H, int64_t Hkv, float base,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* out[S, D] = softmax((x Wq)(x Wk)^T / sqrt(128)) (x Wv) @ Wo per head, heads
+ * of 128 (H = D/128), no mask, no RoPE (mlx/kernels/full/mha_attention.py:13-28);
+ * all four weights (in, out) = [D, D]. */
+size_t mb_mha_attention_workspace_bytes(int64_t S, int64_t D);
+int mb_mha_attention_bf16(const uint16_t* x, const uint16_t* wq, const uint16_t* wk,
+                          const uint16_t* wv, const uint16_t* wo, uint16_t* out, int64_t S,
+                          int64_t D, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Pre-LN transformer block (mlx/kernels/full/transformer_block.py:22-52):
+ * x1 = x + MHA(LN(x)) @ W_o with W_qkv [D, 3D], H heads of 128 (D = 128*H);
+ * out = x1 + gelu(LN(x1) @ W_ff1) @ W_ff2 with W_ff1 [D, FF], W_ff2 [FF, D].
+ * LN has no affine; gelu is the exact x*Phi(x). */
+size_t mb_transformer_block_workspace_bytes(int64_t S, int64_t D, int64_t H, int64_t FF);
+int mb_transformer_block_bf16(const uint16_t* x, const uint16_t* w_qkv, const uint16_t* w_o,
+                              const uint16_t* w_ff1, const uint16_t* w_ff2, uint16_t* out,
+                              int64_t S, int64_t D, int64_t H, int64_t FF, float eps,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* C[b] = A[b] @ B[b] for b < batch, fp32 row-major contiguous batches
  * (mlx/kernels/common/batch_mm.py:10-11, registry.py:61-77, 131), 3xTF32 like
  * mb_sqr_mm_f32. Workspace: mb_batch_mm_f32_workspace_bytes, 256-byte aligned. */

@@ -77,6 +77,11 @@ SIGNATURES = {
     "mb_llama_attention_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64, _I64]),
     "mb_llama_attention_bf16": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, _P,
                                            C.c_size_t, _P]),
+    "mb_mha_attention_workspace_bytes": (C.c_size_t, [_I64, _I64]),
+    "mb_mha_attention_bf16": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _P, C.c_size_t, _P]),
+    "mb_transformer_block_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64, _I64]),
+    "mb_transformer_block_bf16": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                            C.c_float, _P, C.c_size_t, _P]),
     "mb_batch_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64, _I64]),
     "mb_batch_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, C.c_size_t, _P]),
     "mb_conv2d_nhwc_bf16": (C.c_int, [_P, _P, _P] + [_I] * 9 + [_P]),

@@ -57,6 +57,48 @@ __global__ void add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16
   }
 }
 
+// y = (x - mean(x)) * rsqrt(var(x) + eps) per row of D (no affine), one warp
+// per row; mean first, then the variance of (x - mean), both in fp32.
+__global__ void layer_norm_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int M,
+                                  int D, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const uint4* xp = reinterpret_cast<const uint4*>(x + (int64_t)row * D);
+  auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
+  auto hi = [](uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); };
+  float s1 = 0.f;
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 a = xp[c];
+    s1 += lo(a.x) + hi(a.x) + lo(a.y) + hi(a.y) + lo(a.z) + hi(a.z) + lo(a.w) + hi(a.w);
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+  const float mean = s1 / (float)D;
+  float s2 = 0.f;
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 a = xp[c];
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float d0 = lo(aw[m]) - mean, d1 = hi(aw[m]) - mean;
+      s2 += d0 * d0 + d1 * d1;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+  const float rs = rsqrtf(s2 / (float)D + eps);
+  uint4* yp = reinterpret_cast<uint4*>(y + (int64_t)row * D);
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 a = xp[c];
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+      o[m] = gemm::pack_bf16((lo(aw[m]) - mean) * rs, (hi(aw[m]) - mean) * rs);
+    yp[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // RoPE over the full width: thread per (position s, pair i).
 __global__ void rope_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int S, int D,
                             float neg_log2_base_over_half) {
@@ -104,13 +146,14 @@ __global__ void sdpa_tables_kernel(int* bt, int pages, int* start_pos, int* kv_l
   }
 }
 
-// llama_attention step 2: per-head interleaved-pair RoPE (omega_i =
+// Attention step 2 (use_rope = 0: no rotation, the multi-head attention of
+// transformer_block / mha_attention): per-head interleaved-pair RoPE (omega_i =
 // base^(-2i/Dh), positions 0..S-1) on q in place inside qkv [S, ld], and on k
 // into the paged cache layout [S/64 pages][Hkv][64][Dh] of the attention
 // kernels, together with v (copied). One thread per (s, head, pair); heads
 // 0..H-1 are q, H..H+Hkv-1 k, H+Hkv.. v.
 __global__ void attn_rope_scatter_kernel(uint16_t* __restrict__ qkv, int64_t ld, int S, int H,
-                                         int Hkv, float neg_log2_base_over_half,
+                                         int Hkv, int use_rope, float neg_log2_base_over_half,
                                          uint16_t* __restrict__ kc, uint16_t* __restrict__ vc) {
   constexpr int Dh = 128, half = Dh / 2;
   const int heads = H + 2 * Hkv;
@@ -121,7 +164,7 @@ __global__ void attn_rope_scatter_kernel(uint16_t* __restrict__ qkv, int64_t ld,
   const int s = (int)(t / ((int64_t)half * heads));
   uint16_t* src = qkv + (int64_t)s * ld + (int64_t)hd * Dh + 2 * i;
   uint32_t w = *reinterpret_cast<const uint32_t*>(src);
-  if (hd < H + Hkv) {
+  if (use_rope && hd < H + Hkv) {
     const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xFFFF0000u);
     float sn, cs;
     sincosf((float)s * exp2f(neg_log2_base_over_half * (float)i), &sn, &cs);
@@ -294,7 +337,7 @@ extern "C" int mb_llama_attention_bf16(const uint16_t* x, const uint16_t* w_qkv,
   // 2. RoPE on q (in place) and k, K/V into pages; identity page table
   const int64_t n = S * (H + 2 * Hkv) * 64;
   attn_rope_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
-      qkv, nqkv, (int)S, (int)H, (int)Hkv, -log2f(base) / 64.f, kc, vc);
+      qkv, nqkv, (int)S, (int)H, (int)Hkv, 1, -log2f(base) / 64.f, kc, vc);
   MB_CUDA(cudaGetLastError());
   sdpa_tables_kernel<<<1, 256, 0, s>>>(bt, pages, sp, kl, (int)S);
   MB_CUDA(cudaGetLastError());
@@ -304,4 +347,125 @@ extern "C" int mb_llama_attention_bf16(const uint16_t* x, const uint16_t* w_qkv,
   if (rc) return rc;
   // 4. out = o @ W_o
   return mb_gemm_bf16(o, w_o, out, S, D, D, 1, stream);
+}
+
+// ---- multi-head attention without RoPE: mha_attention
+//      (mlx/kernels/full/mha_attention.py:13-28) and transformer_block
+//      (mlx/kernels/full/transformer_block.py:22-52) --------------------------
+namespace {
+struct MhaWs {
+  size_t qkv, kc, o, tables, total;
+};
+MhaWs mha_ws(int64_t S, int64_t D, int64_t H) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const int64_t pages = (S + 63) / 64;
+  MhaWs w;
+  w.qkv = al((size_t)S * 3 * D * 2);
+  w.kc = al((size_t)pages * H * 64 * 128 * 2);
+  w.o = al((size_t)S * D * 2);
+  w.tables = al((size_t)(pages + 2) * 4);
+  w.total = w.qkv + 2 * w.kc + w.o + w.tables;
+  return w;
+}
+
+// attention of the packed qkv [S, 3D] (q | k | v, H heads of 128 each, no
+// RoPE, no mask) into o [S, D]; kc, vc, tables from the workspace layout above
+int mha_core(uint16_t* qkv, uint8_t* w, const MhaWs& wl, int64_t S, int64_t D, int64_t H,
+             uint16_t* o, cudaStream_t s) {
+  uint16_t* kc = reinterpret_cast<uint16_t*>(w + wl.qkv);
+  uint16_t* vc = reinterpret_cast<uint16_t*>(w + wl.qkv + wl.kc);
+  int* bt = reinterpret_cast<int*>(w + wl.qkv + 2 * wl.kc + wl.o);
+  const int pages = (int)((S + 63) / 64);
+  int* sp = bt + pages;
+  int* kl = sp + 1;
+  const int64_t n = S * 3 * H * 64;
+  attn_rope_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+      qkv, 3 * D, (int)S, (int)H, (int)H, 0, 0.f, kc, vc);
+  MB_CUDA(cudaGetLastError());
+  sdpa_tables_kernel<<<1, 256, 0, s>>>(bt, pages, sp, kl, (int)S);
+  MB_CUDA(cudaGetLastError());
+  return mb_attention_prefill_bf16(qkv, (int)(3 * D), kc, vc, bt, pages, sp, kl, 1, (int)S,
+                                   (int)H, (int)H, 128, 0, o, (int)D, s);
+}
+}  // namespace
+
+extern "C" size_t mb_mha_attention_workspace_bytes(int64_t S, int64_t D) {
+  if (S <= 0 || D <= 0 || D % 128) return 0;
+  return mha_ws(S, D, D / 128).total;
+}
+
+extern "C" int mb_mha_attention_bf16(const uint16_t* x, const uint16_t* wq, const uint16_t* wk,
+                                     const uint16_t* wv, const uint16_t* wo, uint16_t* out,
+                                     int64_t S, int64_t D, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  MB_REQUIRE(S >= 0 && D > 0 && D % 128 == 0, "mha_attention: D must be a multiple of 128");
+  if (S == 0) return MB_OK;
+  MB_REQUIRE(S <= (1 << 24), "mha_attention: S too large");
+  const int64_t H = D / 128;
+  const MhaWs wl = mha_ws(S, D, H);
+  MB_REQUIRE(workspace && workspace_bytes >= wl.total,
+             "mha_attention: workspace of %zu bytes required", wl.total);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  uint16_t* qkv = reinterpret_cast<uint16_t*>(w);
+  uint16_t* o = reinterpret_cast<uint16_t*>(w + wl.qkv + 2 * wl.kc);
+  // q | k | v side by side in one [S, 3D] buffer
+  const uint16_t* ws3[3] = {wq, wk, wv};
+  for (int j = 0; j < 3; ++j) {
+    const int rc = mb::gemm_bf16_ex(x, ws3[j], qkv + j * D, S, D, D, 3 * D, 1, nullptr, 0, 0, s);
+    if (rc) return rc;
+  }
+  const int rc = mha_core(qkv, w, wl, S, D, H, o, s);
+  if (rc) return rc;
+  return mb::gemm_bf16_ex(o, wo, out, S, D, D, D, 1, nullptr, 0, 0, s);
+}
+
+namespace {
+size_t tb_extra(int64_t S, int64_t D, int64_t FF) {  // ln, x1, ffn hidden
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  return 2 * al((size_t)S * D * 2) + al((size_t)S * FF * 2);
+}
+}  // namespace
+
+extern "C" size_t mb_transformer_block_workspace_bytes(int64_t S, int64_t D, int64_t H,
+                                                       int64_t FF) {
+  if (S <= 0 || D <= 0 || H <= 0 || FF <= 0 || D != 128 * H) return 0;
+  return mha_ws(S, D, H).total + tb_extra(S, D, FF);
+}
+
+extern "C" int mb_transformer_block_bf16(const uint16_t* x, const uint16_t* w_qkv,
+                                         const uint16_t* w_o, const uint16_t* w_ff1,
+                                         const uint16_t* w_ff2, uint16_t* out, int64_t S,
+                                         int64_t D, int64_t H, int64_t FF, float eps,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  MB_REQUIRE(S >= 0 && H > 0 && D == 128 * H && D % 8 == 0 && FF > 0 && FF % 8 == 0,
+             "transformer_block: need D = 128 * H and FF a multiple of 8");
+  if (S == 0) return MB_OK;
+  MB_REQUIRE(S <= (1 << 24), "transformer_block: S too large");
+  const MhaWs wl = mha_ws(S, D, H);
+  const size_t need = wl.total + tb_extra(S, D, FF);
+  MB_REQUIRE(workspace && workspace_bytes >= need,
+             "transformer_block: workspace of %zu bytes required", need);
+  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  uint16_t* qkv = reinterpret_cast<uint16_t*>(w);
+  uint16_t* o = reinterpret_cast<uint16_t*>(w + wl.qkv + 2 * wl.kc);
+  uint16_t* ln = reinterpret_cast<uint16_t*>(w + wl.total);
+  uint16_t* x1 = reinterpret_cast<uint16_t*>(w + wl.total + al((size_t)S * D * 2));
+  uint16_t* hdn = reinterpret_cast<uint16_t*>(w + wl.total + 2 * al((size_t)S * D * 2));
+  const unsigned ln_grid = (unsigned)((S + 7) / 8);
+  // attention sub-block: x1 = x + MHA(LN(x)) @ W_o
+  layer_norm_kernel<<<ln_grid, 256, 0, s>>>(x, ln, (int)S, (int)D, eps);
+  MB_CUDA(cudaGetLastError());
+  int rc = mb::gemm_bf16_ex(ln, w_qkv, qkv, S, 3 * D, D, 3 * D, 1, nullptr, 0, 0, s);
+  if (!rc) rc = mha_core(qkv, w, wl, S, D, H, o, s);
+  if (!rc) rc = mb::gemm_bf16_ex(o, w_o, x1, S, D, D, D, 1, x, D, 0, s);
+  if (rc) return rc;
+  // FFN sub-block: out = x1 + gelu(LN(x1) @ W_ff1) @ W_ff2
+  layer_norm_kernel<<<ln_grid, 256, 0, s>>>(x1, ln, (int)S, (int)D, eps);
+  MB_CUDA(cudaGetLastError());
+  rc = mb::gemm_bf16_ex(ln, w_ff1, hdn, S, FF, D, FF, 1, nullptr, 0, 1, s);
+  if (!rc) rc = mb::gemm_bf16_ex(hdn, w_ff2, out, S, D, FF, D, 1, x1, D, 0, s);
+  return rc;
 }

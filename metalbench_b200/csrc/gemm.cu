@@ -12,6 +12,24 @@
 
 using namespace gemm;
 
+namespace mb {
+int gemm_bf16_ex(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N,
+                 int64_t K, int64_t ldc, int b_layout, const uint16_t* residual, int64_t ld_res,
+                 int act, cudaStream_t s) {
+  gemm::Epi<256, gemm::EpiStore> e{};
+  e.M = (int)M;
+  e.N = (int)N;
+  e.out = C;
+  e.ldo = ldc;
+  e.alpha = 1.f;
+  e.residual = residual;
+  e.ld_res = ld_res;
+  e.act = act;
+  if (b_layout == 0) return launch_gemm<gemm::Mode::BF16, 256, 4, false>(A, B, e, M, N, K, 1, s);
+  return launch_gemm<gemm::Mode::BF16, 256, 4, true>(A, B, e, M, N, K, 1, s);
+}
+}  // namespace mb
+
 extern "C" int mb_gemm_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M,
                             int64_t N, int64_t K, int b_layout, void* stream) {
   MB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "mb_gemm_bf16: negative dimension");
@@ -19,15 +37,8 @@ extern "C" int mb_gemm_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, i
   if (M == 0 || N == 0) return MB_OK;
   MB_REQUIRE(K > 0, "mb_gemm_bf16: K must be positive");
   MB_REQUIRE(N % 8 == 0, "mb_gemm_bf16: N must be a multiple of 8");
-  gemm::Epi<256, gemm::EpiStore> e{};
-  e.M = (int)M;
-  e.N = (int)N;
-  e.out = C;
-  e.ldo = N;
-  e.alpha = 1.f;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (b_layout == 0) return launch_gemm<gemm::Mode::BF16, 256, 4, false>(A, B, e, M, N, K, 1, s);
-  return launch_gemm<gemm::Mode::BF16, 256, 4, true>(A, B, e, M, N, K, 1, s);
+  return mb::gemm_bf16_ex(A, B, C, M, N, K, N, b_layout, nullptr, 0, 0,
+                          static_cast<cudaStream_t>(stream));
 }
 
 // k-blocks (32 fp32 of K each) per tensor-core partial sum of the 3xTF32

@@ -94,7 +94,7 @@ __device__ __forceinline__ void storeW_bf16(uint16_t* p, const float (&v)[W]) {
   }
 }
 
-// out[row, n] = alpha * row_scale[row] * acc[row, n] (+ residual[row, n]),
+// out[row, n] = act(alpha * row_scale[row] * acc[row, n]) (+ residual[row, n]),
 // stored as bf16 or fp32. row_scale and residual are optional (null).
 struct EpiStore {
   int M, N;
@@ -105,11 +105,16 @@ struct EpiStore {
   const float* row_scale;
   const uint16_t* residual;  // bf16 [M, ld_res]
   int64_t ld_res;
+  int act;  // 0: none; 1: exact GELU x*Phi(x), applied after the scale, before the residual
   // Scale, add the residual and store 32 accumulator values of row c.row
   // starting at column n.
   __device__ void finish32(const EpiCtx& c, float sc, int n, float (&v)[32]) const {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= sc;
+    if (act == 1) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
+    }
     if (residual) {
       const uint16_t* r = residual + (int64_t)c.row * ld_res + n;
       if (n + 32 <= N && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {

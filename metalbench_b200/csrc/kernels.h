@@ -62,6 +62,11 @@ int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream);
 int tp_world();
 int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 
+// gemm.cu: bf16 GEMM C[M, N] (row stride ldc) = act(A @ B) (+ residual, row
+// stride ld_res); b_layout 0: B [N, K], 1: B [K, N]; act 0 none, 1 exact GELU.
+int gemm_bf16_ex(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N,
+                 int64_t K, int64_t ldc, int b_layout, const uint16_t* residual, int64_t ld_res,
+                 int act, cudaStream_t s);
 // decoder.cu helpers shared with fused_ops.cu
 int rownorm(const uint16_t* x, int M, int D, float eps, float* rstd, cudaStream_t s);
 int pack_tiled_weight(const uint16_t* in, int64_t ld_in, int K, const int* col_idx_dev, int Nout,

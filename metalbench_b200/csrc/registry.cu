@@ -489,6 +489,84 @@ int prep_llama_attention(const RunArgs& a, KernelState& st, cudaStream_t) {
   return MB_OK;
 }
 
+// mha_attention: full/registry.py:107-130 — x@0 [S, D], wq@1, wk@2, wv@3,
+// wo@4 [D, D], out@5; S@6, D@7, H@8, Dh@9, scale@10. Heads of 128: H = D/128.
+int prep_mha(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *wq, *wk, *wv, *wo, *o;
+  int64_t S, D, H = 0;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &wq));
+  TRY(need_buf(a, 2, MB_ROLE_INPUT, &wk));
+  TRY(need_buf(a, 3, MB_ROLE_INPUT, &wv));
+  TRY(need_buf(a, 4, MB_ROLE_INPUT, &wo));
+  TRY(need_buf(a, 5, MB_ROLE_OUTPUT, &o));
+  TRY(need_scalar(a, 6, &S));
+  TRY(need_scalar(a, 7, &D));
+  TRY(bf16_all({x, wq, wk, wv, wo, o}, "mha_attention"));
+  double h = 0;
+  if (a.scalar(8, &h)) H = (int64_t)h;
+  MB_REQUIRE(D % 128 == 0 && (H == 0 || H == D / 128),
+             "mha_attention: heads of 128 required (H = D/128)");
+  MB_REQUIRE(x->bytes == (size_t)(S * D * 2) && o->bytes == x->bytes &&
+                 wq->bytes == (size_t)(D * D * 2) && wk->bytes == wq->bytes &&
+                 wv->bytes == wq->bytes && wo->bytes == wq->bytes,
+             "mha_attention: buffer sizes do not match S/D");
+  const size_t wsb = mb_mha_attention_workspace_bytes(S, D);
+  void* ws = nullptr;
+  MB_CUDA(cudaMalloc(&ws, wsb));
+  st.scratch.push_back(ws);
+  const void *px = x->dev, *pq = wq->dev, *pk = wk->dev, *pv = wv->dev, *pw = wo->dev;
+  void* po = o->dev;
+  st.launches_per_iter = 7;
+  st.launch = [=](cudaStream_t s) {
+    return mb_mha_attention_bf16((const uint16_t*)px, (const uint16_t*)pq, (const uint16_t*)pk,
+                                 (const uint16_t*)pv, (const uint16_t*)pw, (uint16_t*)po, S, D,
+                                 ws, wsb, s);
+  };
+  return MB_OK;
+}
+
+// transformer_block: full/registry.py:47-62 — x@0 [S, D], W_qkv@1 [D, 3D],
+// W_o@2 [D, D], W_ff1@3 [D, FF], W_ff2@4 [FF, D], out@5; S@6, D@7, H@8, FF@9,
+// eps@10 (f32).
+int prep_transformer_block(const RunArgs& a, KernelState& st, cudaStream_t) {
+  const RunArgs::Buf *x, *wqkv, *wo, *w1, *w2, *o;
+  int64_t S, D, H, FF;
+  TRY(need_buf(a, 0, MB_ROLE_INPUT, &x));
+  TRY(need_buf(a, 1, MB_ROLE_INPUT, &wqkv));
+  TRY(need_buf(a, 2, MB_ROLE_INPUT, &wo));
+  TRY(need_buf(a, 3, MB_ROLE_INPUT, &w1));
+  TRY(need_buf(a, 4, MB_ROLE_INPUT, &w2));
+  TRY(need_buf(a, 5, MB_ROLE_OUTPUT, &o));
+  TRY(need_scalar(a, 6, &S));
+  TRY(need_scalar(a, 7, &D));
+  TRY(need_scalar(a, 8, &H));
+  TRY(need_scalar(a, 9, &FF));
+  double eps = 1e-5;
+  a.scalar(10, &eps);
+  TRY(bf16_all({x, wqkv, wo, w1, w2, o}, "transformer_block"));
+  MB_REQUIRE(H > 0 && D == 128 * H, "transformer_block: heads of 128 required (D = 128*H)");
+  MB_REQUIRE(x->bytes == (size_t)(S * D * 2) && o->bytes == x->bytes &&
+                 wqkv->bytes == (size_t)(3 * D * D * 2) && wo->bytes == (size_t)(D * D * 2) &&
+                 w1->bytes == (size_t)(D * FF * 2) && w2->bytes == w1->bytes,
+             "transformer_block: buffer sizes do not match S/D/FF");
+  const size_t wsb = mb_transformer_block_workspace_bytes(S, D, H, FF);
+  void* ws = nullptr;
+  MB_CUDA(cudaMalloc(&ws, wsb));
+  st.scratch.push_back(ws);
+  const void *px = x->dev, *p1 = wqkv->dev, *p2 = wo->dev, *p3 = w1->dev, *p4 = w2->dev;
+  void* po = o->dev;
+  const float fe = (float)eps;
+  st.launches_per_iter = 10;
+  st.launch = [=](cudaStream_t s) {
+    return mb_transformer_block_bf16((const uint16_t*)px, (const uint16_t*)p1,
+                                     (const uint16_t*)p2, (const uint16_t*)p3,
+                                     (const uint16_t*)p4, (uint16_t*)po, S, D, H, FF, fe, ws, wsb,
+                                     s);
+  };
+  return MB_OK;
+}
+
 }  // namespace
 
 void register_all_kernels() {
@@ -507,6 +585,8 @@ void register_all_kernels() {
     register_kernel({"swiglu", prep_swiglu});
     register_kernel({"scaled_dot_product", prep_sdpa});
     register_kernel({"llama_attention", prep_llama_attention});
+    register_kernel({"mha_attention", prep_mha});
+    register_kernel({"transformer_block", prep_transformer_block});
   });
 }
 

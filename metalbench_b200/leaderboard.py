@@ -41,6 +41,8 @@ KERNEL_SOURCES = {
     "swiglu": ["fused_ops.cu", "decoder_epi.cuh", "gemm_core.cuh"],
     "scaled_dot_product": ["fused_ops.cu", "attention.cu"],
     "llama_attention": ["fused_ops.cu", "attention.cu", "gemm.cu"],
+    "mha_attention": ["fused_ops.cu", "attention.cu", "gemm.cu"],
+    "transformer_block": ["fused_ops.cu", "attention.cu", "gemm.cu", "gemm_epi.cuh"],
 }
 # files every kernel depends on
 SHARED_SOURCES = ["common.cuh", "abi.cu", "registry.cu", "kernels.h"]

@@ -36,6 +36,10 @@ def mean(a, axis=None, keepdims=False):
     return np.mean(a, axis=axis, keepdims=keepdims, dtype=a.dtype)
 
 
+def var(a, axis=None, keepdims=False, ddof=0):
+    return np.var(a, axis=axis, keepdims=keepdims, ddof=ddof, dtype=a.dtype)
+
+
 def rsqrt(a):
     return (1.0 / np.sqrt(a)).astype(np.asarray(a).dtype)
 

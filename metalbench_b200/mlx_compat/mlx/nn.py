@@ -14,6 +14,12 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
+def gelu(x):
+    """Exact GELU, x * Phi(x) = 0.5 x (1 + erf(x / sqrt(2))) (MLX nn.gelu)."""
+    from scipy.special import erf
+    return (0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))).astype(np.asarray(x).dtype)
+
+
 class RMSNorm(Module):
     """x * rsqrt(mean(x^2, -1) + eps) * weight, weight initialised to ones."""
 

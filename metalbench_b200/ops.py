@@ -249,3 +249,38 @@ def llama_attention(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, n_h
     _lib.call("mb_llama_attention_bf16", x.data_ptr(), w_qkv.data_ptr(), w_o.data_ptr(),
               out.data_ptr(), S, D, n_heads, n_kv_heads, base, ws.data_ptr(), nb, _stream())
     return out
+
+
+def mha_attention(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor,
+                  wo: torch.Tensor) -> torch.Tensor:
+    """Multi-head self-attention of x [S, D] with heads of 128 (bf16, no mask,
+    no RoPE), weights (in, out) [D, D]."""
+    for n, t in (("x", x), ("wq", wq), ("wk", wk), ("wv", wv), ("wo", wo)):
+        _cuda(t, f"mha_attention({n})", (torch.bfloat16,))
+    init(x.device.index)
+    S, D = x.shape
+    out = torch.empty((S, D), dtype=torch.bfloat16, device=x.device)
+    nb = _lib.lib().mb_mha_attention_workspace_bytes(S, D)
+    ws = _workspace(nb, x.device)
+    _lib.call("mb_mha_attention_bf16", x.data_ptr(), wq.data_ptr(), wk.data_ptr(), wv.data_ptr(),
+              wo.data_ptr(), out.data_ptr(), S, D, ws.data_ptr(), nb, _stream())
+    return out
+
+
+def transformer_block(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor,
+                      w_ff1: torch.Tensor, w_ff2: torch.Tensor, n_heads: int,
+                      eps: float = 1e-5) -> torch.Tensor:
+    """Pre-LN block y = x1 + gelu(LN(x1) W_ff1) W_ff2, x1 = x + MHA(LN(x)) W_o
+    (bf16, heads of 128, weights (in, out))."""
+    for n, t in (("x", x), ("w_qkv", w_qkv), ("w_o", w_o), ("w_ff1", w_ff1), ("w_ff2", w_ff2)):
+        _cuda(t, f"transformer_block({n})", (torch.bfloat16,))
+    init(x.device.index)
+    S, D = x.shape
+    FF = w_ff1.shape[1]
+    out = torch.empty((S, D), dtype=torch.bfloat16, device=x.device)
+    nb = _lib.lib().mb_transformer_block_workspace_bytes(S, D, n_heads, FF)
+    ws = _workspace(nb, x.device)
+    _lib.call("mb_transformer_block_bf16", x.data_ptr(), w_qkv.data_ptr(), w_o.data_ptr(),
+              w_ff1.data_ptr(), w_ff2.data_ptr(), out.data_ptr(), S, D, n_heads, FF, eps,
+              ws.data_ptr(), nb, _stream())
+    return out

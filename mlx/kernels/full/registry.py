@@ -52,3 +52,39 @@ REGISTRY["llama_decoder_layer_decode"] = dict(
     flops=2 * _PARAMS * _BD + 2 * 2 * _BD * H * DH * (_L + 1),
     bytes=2 * _PARAMS + 2 * 2 * _BD * HKV * _L * DH,
     roof="hbm", ref_warmup=0, ref_iters=2)
+
+# transformer_block (reference full/registry.py:47-62: S 64, D 128, 4 heads of
+# 32, FF 256, fp32) at a BERT-large-like B200 shape: S 4096, d_model 4096, 32
+# heads of 128, FF 16384, bf16.
+TB_S, TB_D, TB_H, TB_FF = 4096, 4096, 32, 16384
+REGISTRY["transformer_block"] = dict(
+    kernel="transformer_block", metal_function="transformer_block_f32",
+    input_bindings=(0, 1, 2, 3, 4),
+    input_shapes=[(TB_S, TB_D), (TB_D, 3 * TB_D), (TB_D, TB_D), (TB_D, TB_FF), (TB_FF, TB_D)],
+    input_dtypes=["bf16"] * 5, input_init=[("normal", 1.0)] + [("normal", 0.02)] * 4,
+    output_shape=(TB_S, TB_D), output_dtype="bf16",
+    scalars=[dict(binding=6, dtype="u32", value=TB_S), dict(binding=7, dtype="u32", value=TB_D),
+             dict(binding=8, dtype="u32", value=TB_H), dict(binding=9, dtype="u32", value=TB_FF),
+             dict(binding=10, dtype="f32", value=1e-5)],
+    model_kwargs=dict(S=TB_S, D=TB_D, H=TB_H, FF=TB_FF, eps=1e-5),
+    rtol=2e-2, atol=2e-2, seed=3,
+    flops=2 * TB_S * TB_D * (4 * TB_D + 2 * TB_FF) + 4 * TB_H * TB_S * TB_S * 128,
+    bytes=2 * (2 * TB_S * TB_D + 4 * TB_D * TB_D + 2 * TB_D * TB_FF),
+    roof="tensor_bf16", ref_warmup=0, ref_iters=1)
+
+# mha_attention (reference full/registry.py:107-130: S 32, D 128, 4 heads of
+# 32, fp32; the hook fixes H = 4) with heads of 128: S 4096, D 512, bf16.
+MHA_S, MHA_D = 4096, 512
+REGISTRY["mha_attention"] = dict(
+    kernel="mha_attention", metal_function="mha_attention_f32",
+    input_bindings=(0, 1, 2, 3, 4),
+    input_shapes=[(MHA_S, MHA_D)] + [(MHA_D, MHA_D)] * 4,
+    input_dtypes=["bf16"] * 5, input_init=[("normal", 1.0)] + [("normal", 0.05)] * 4,
+    output_shape=(MHA_S, MHA_D), output_dtype="bf16",
+    scalars=[dict(binding=6, dtype="u32", value=MHA_S), dict(binding=7, dtype="u32", value=MHA_D),
+             dict(binding=8, dtype="u32", value=4), dict(binding=9, dtype="u32", value=128),
+             dict(binding=10, dtype="f32", value=0.08838834764831845)],
+    rtol=2e-2, atol=2e-2, seed=3,
+    flops=2 * MHA_S * MHA_D * MHA_D * 4 + 4 * MHA_S * MHA_S * MHA_D,
+    bytes=2 * (2 * MHA_S * MHA_D + 4 * MHA_D * MHA_D), roof="tensor_bf16",
+    ref_warmup=0, ref_iters=1)

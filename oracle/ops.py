@@ -298,3 +298,48 @@ def llama_attention(x, W_qkv, W_o, *, H: int, H_kv: int, base: float = 10000.0,
     p = p / p.sum(axis=-1, keepdims=True)
     o = (p @ v).transpose(1, 0, 2).reshape(S, D)
     return (o @ W_o.astype(acc)).astype(np.float32)
+
+
+def layer_norm(x, eps=1e-5):
+    """(x - mean) / sqrt(var + eps) over the last axis, no affine, ddof 0
+    (mlx/kernels/full/transformer_block.py:49-52)."""
+    m = x.mean(axis=-1, keepdims=True)
+    v = ((x - m) ** 2).mean(axis=-1, keepdims=True)
+    return (x - m) / np.sqrt(v + eps)
+
+
+def gelu(x):
+    """Exact GELU x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)) (MLX nn.gelu)."""
+    from scipy.special import erf
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+def _mha(x, W_q, W_k, W_v, H):
+    S, D = x.shape
+    Dh = D // H
+    q = (x @ W_q).reshape(S, H, Dh).transpose(1, 0, 2)
+    k = (x @ W_k).reshape(S, H, Dh).transpose(1, 0, 2)
+    v = (x @ W_v).reshape(S, H, Dh).transpose(1, 0, 2)
+    sc = q @ k.transpose(0, 2, 1) / np.sqrt(x.dtype.type(Dh))
+    sc = sc - sc.max(axis=-1, keepdims=True)
+    p = np.exp(sc)
+    p = p / p.sum(axis=-1, keepdims=True)
+    return (p @ v).transpose(1, 0, 2).reshape(S, D)
+
+
+def mha_attention(x, wq, wk, wv, wo, *, H: int = 4, acc=np.float64):
+    """Multi-head attention, H heads of D/H, no mask (mlx/kernels/full/mha_attention.py:13-28)."""
+    f = lambda a: a.astype(acc)
+    return (_mha(f(x), f(wq), f(wk), f(wv), H) @ f(wo)).astype(np.float32)
+
+
+def transformer_block(x, W_qkv, W_o, W_ff1, W_ff2, *, H: int, eps: float = 1e-5, acc=np.float64):
+    """Pre-LN block (mlx/kernels/full/transformer_block.py:22-47):
+    x1 = x + MHA(LN(x)) @ W_o with W_qkv = [Wq | Wk | Wv]; y = x1 + gelu(LN(x1) @ W_ff1) @ W_ff2."""
+    x = x.astype(acc)
+    D = x.shape[1]
+    Wqkv = W_qkv.astype(acc)
+    ln1 = layer_norm(x, eps)
+    x1 = x + _mha(ln1, Wqkv[:, :D], Wqkv[:, D:2 * D], Wqkv[:, 2 * D:], H) @ W_o.astype(acc)
+    ff = gelu(layer_norm(x1, eps) @ W_ff1.astype(acc)) @ W_ff2.astype(acc)
+    return (x1 + ff).astype(np.float32)

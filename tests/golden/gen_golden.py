@@ -46,6 +46,8 @@ CASES = [
     ("rect_mm", "common", [(32, 96), (96, 40)], 5),
     ("batch_mm", "common", [(3, 16, 24), (3, 24, 20)], 5),
     ("llama_attention", "standard", [(64, 128), (128, 256), (128, 128)], 5),
+    ("transformer_block", "full", [(64, 128), (128, 384), (128, 128), (128, 256), (256, 128)], 5),
+    ("mha_attention", "full", [(32, 128)] + [(128, 128)] * 4, 5),
 ]
 
 

@@ -126,3 +126,29 @@ def test_llama_attention(S, H, Hkv):
     got = ops.llama_attention(_bf(torch, x), _bf(torch, wqkv), _bf(torch, wo), H, Hkv)
     # q/k/v and the attention output pass through bf16 between the four steps
     _check(_np(got), O.llama_attention(x, wqkv, wo, H=H, H_kv=Hkv), frac=0.999)
+
+
+@pytest.mark.parametrize("S,D", [(512, 512), (200, 256), (1024, 1024), (64, 128)])
+def test_mha_attention(S, D):
+    """Three projections into one [S, 3D] buffer -> MHA (heads of 128, no RoPE) -> @ wo."""
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(17)
+    x = _r(rng, S, D)
+    ws = [_r(rng, D, D, scale=D ** -0.5) for _ in range(4)]
+    got = ops.mha_attention(_bf(torch, x), *[_bf(torch, w) for w in ws])
+    _check(_np(got), O.mha_attention(x, *ws, H=D // 128), frac=0.999)
+
+
+@pytest.mark.parametrize("S,H,FF", [(512, 4, 1024), (300, 2, 512), (256, 8, 4096)])
+def test_transformer_block(S, H, FF):
+    """LN -> QKV -> MHA -> W_o + residual -> LN -> W_ff1 + exact GELU -> W_ff2 + residual."""
+    import torch
+    from metalbench_b200 import ops
+    rng = np.random.default_rng(18)
+    D = 128 * H
+    x = _r(rng, S, D)
+    w = [_r(rng, D, 3 * D, scale=D ** -0.5), _r(rng, D, D, scale=D ** -0.5),
+         _r(rng, D, FF, scale=D ** -0.5), _r(rng, FF, D, scale=FF ** -0.5)]
+    got = ops.transformer_block(_bf(torch, x), *[_bf(torch, t) for t in w], H)
+    _check(_np(got), O.transformer_block(x, *w, H=H), frac=0.999)

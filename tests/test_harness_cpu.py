@@ -128,6 +128,7 @@ def test_grade_targets():
                                       ("rope_embedding", 1), ("swiglu", 3),
                                       ("scaled_dot_product", 3), ("fused_qkv_projection", 2),
                                       ("rect_mm", 2), ("batch_mm", 2), ("llama_attention", 3), ("sqr_mm", 2),
+                                      ("transformer_block", 5), ("mha_attention", 5),
                                       ("transpose_2d", 1)])
 def test_our_hooks_reproduce_reference_hooks(name, nin):
     """Each hook under mlx/kernels/ (default arguments) reproduces the golden

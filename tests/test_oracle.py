@@ -112,6 +112,8 @@ def test_allclose_report_fraction():
     ("rect_mm", lambda d: O.sqr_mm(d["in0"], d["in1"])),
     ("batch_mm", lambda d: O.sqr_mm(d["in0"], d["in1"])),
     ("llama_attention", lambda d: O.llama_attention(d["in0"], d["in1"], d["in2"], H=4, H_kv=2)),
+    ("transformer_block", lambda d: O.transformer_block(*[d[f"in{i}"] for i in range(5)], H=4)),
+    ("mha_attention", lambda d: O.mha_attention(*[d[f"in{i}"] for i in range(5)], H=4)),
 ])
 def test_standard_set_oracle_matches_reference_hooks(name, fn):
     d = _load(name)
