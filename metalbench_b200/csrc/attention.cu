@@ -15,10 +15,13 @@
 //    head (the 16 rows of a warp MMA), so every K/V byte is read once; whole
 //    16 KiB pages stream into shared memory through a cp.async ring; partial
 //    (max, sum, o) triples are merged by a small combine kernel.
-//  * prefill: FlashAttention-2 style tiles on the warp-level bf16 tensor-core
-//    MMA (mma.sync m16n8k16), 64 queries x 64 keys per step, online softmax in
-//    fp32, causal skip of key tiles above the diagonal.
+//  * prefill: tcgen05/TMEM kernel in attention_tc.cu when TMA can address the
+//    operands (16-byte aligned rows); otherwise FlashAttention-2 style tiles
+//    on the warp-level bf16 MMA (mma.sync m16n8k16) below, 64 queries x 64
+//    keys per step, online softmax in fp32, causal skip of key tiles above
+//    the diagonal.
 #include "common.cuh"
+#include "kernels.h"
 
 namespace {
 
@@ -531,9 +534,13 @@ extern "C" int mb_attention_prefill_bf16(const uint16_t* q, int ldq, const uint1
   MB_REQUIRE(ldq % 2 == 0 && ldo % 2 == 0, "attention: leading dimensions must be even");
   if (B == 0 || S == 0) return MB_OK;
   MB_REQUIRE(Hq <= 65535 && B <= 65535, "attention: grid too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // tcgen05 kernel (attention_tc.cu) whenever TMA can address the operands
+  if (mb::attention_prefill_tc_ok(q, ldq, k_cache, v_cache, out, ldo))
+    return mb::attention_prefill_tc(q, ldq, k_cache, v_cache, block_table, max_pages, start_pos,
+                                    kv_len, B, S, Hq, Hkv, causal, out, ldo, s);
   const int smem = 4 * PAGE * KV_LD * 2;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)DH);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid((S + 63) / 64, Hq, B);
   static bool attr = false;
   if (!attr) {

@@ -67,6 +67,15 @@ int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 int gemm_bf16_ex(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N,
                  int64_t K, int64_t ldc, int b_layout, const uint16_t* residual, int64_t ld_res,
                  int act, cudaStream_t s);
+// attention_tc.cu: tcgen05 prefill attention (same contract as
+// mb_attention_prefill_bf16, Dh = 128); _ok() says whether TMA can address
+// the operands.
+bool attention_prefill_tc_ok(const uint16_t* q, int ldq, const uint16_t* k_cache,
+                             const uint16_t* v_cache, uint16_t* out, int ldo);
+int attention_prefill_tc(const uint16_t* q, int ldq, const uint16_t* k_cache,
+                         const uint16_t* v_cache, const int* block_table, int max_pages,
+                         const int* start_pos, const int* kv_len, int B, int S, int Hq, int Hkv,
+                         int causal, uint16_t* out, int ldo, cudaStream_t stream);
 // decoder.cu helpers shared with fused_ops.cu
 int rownorm(const uint16_t* x, int M, int D, float eps, float* rstd, cudaStream_t s);
 int pack_tiled_weight(const uint16_t* in, int64_t ld_in, int K, const int* col_idx_dev, int Nout,
