@@ -158,7 +158,8 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    uint32_t used = 0;  // bit st: slot st received loads; bit 2+st: the parity of the last
+    // per ring: bit st = slot st received a load, bit 2+st = that load's parity
+    uint32_t used_k = 0, used_v = 0;
     if (lane == 0) {
       mbd::prefetch_tmap(&p.qmap);
       mbd::prefetch_tmap(&p.kmap);
@@ -180,21 +181,33 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
           mbd::tma_load_2d(dst + c * CHUNK + pi * HALF_PAGE, map, bar, c * 64, row);
       }
     };
+    // K runs one tile ahead of V: K_{j+1} is requested before V_j, since a K
+    // slot frees up (S done) about a tile before a V slot (P V done) and a
+    // load takes about a tile to land.
     bool ok = true;
+    if (n_tiles > 0) {
+      if (lane == 0) load_tile(0, &p.kmap, base + OFF_K, &kfull[0]);
+      __syncwarp();
+      used_k = 1u;
+    }
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int st = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      ok = __all_sync(0xffffffffu, mbd::mbar_wait(&kempty[st], ph ^ 1, status,
-                                                  MB_DEV_TIMEOUT_TMA, abort_flag));
-      if (!ok) break;
-      if (lane == 0) load_tile(j, &p.kmap, base + OFF_K + st * TILE, &kfull[st]);
-      __syncwarp();
+      if (j + 1 < n_tiles) {
+        const int kst = (j + 1) & 1;
+        ok = __all_sync(0xffffffffu, mbd::mbar_wait(&kempty[kst], (((j + 1) >> 1) & 1) ^ 1,
+                                                    status, MB_DEV_TIMEOUT_TMA, abort_flag));
+        if (!ok) break;
+        if (lane == 0) load_tile(j + 1, &p.kmap, base + OFF_K + kst * TILE, &kfull[kst]);
+        __syncwarp();
+        used_k = (used_k & ~(5u << kst)) | (1u << kst) | ((((j + 1) >> 1) & 1) << (2 + kst));
+      }
       ok = __all_sync(0xffffffffu, mbd::mbar_wait(&vempty[st], ph ^ 1, status,
                                                   MB_DEV_TIMEOUT_TMA, abort_flag));
       if (!ok) break;
       if (lane == 0) load_tile(j, &p.vmap, base + OFF_V + st * TILE, &vfull[st]);
       __syncwarp();
-      used = (used & ~(5u << st)) | (1u << st) | (ph << (2 + st));
+      used_v = (used_v & ~(5u << st)) | (1u << st) | (ph << (2 + st));
     }
     // V rows past kv_len in the last tile (unloaded pages, or the rest of a
     // partial page) must be finite: P is 0 there, but 0 * NaN is not.
@@ -222,10 +235,12 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
     if (lane == 0) {
       mbd::mbar_wait(q_full, 0, status, MB_DEV_TIMEOUT_TMA);
       for (int st = 0; st < 2; ++st)
-        if (used & (1u << st)) {
-          mbd::mbar_wait(&kfull[st], (used >> (2 + st)) & 1, status, MB_DEV_TIMEOUT_TMA);
-          mbd::mbar_wait(&vfull[st], (used >> (2 + st)) & 1, status, MB_DEV_TIMEOUT_TMA);
-        }
+      {
+        if (used_k & (1u << st))
+          mbd::mbar_wait(&kfull[st], (used_k >> (2 + st)) & 1, status, MB_DEV_TIMEOUT_TMA);
+        if (used_v & (1u << st))
+          mbd::mbar_wait(&vfull[st], (used_v >> (2 + st)) & 1, status, MB_DEV_TIMEOUT_TMA);
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -324,17 +339,21 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
       float mx[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
+      if (full) {  // the common case: no per-key compare at all
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float x = __uint_as_float(s[c][e]);
-          if (!full && kbase + c * 16 + e > kmax) {
-            x = -INFINITY;
-            s[c][e] = __float_as_uint(x);
+          for (int e = 0; e < 16; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(s[c][e]));
+      } else {
+        const int lim = kmax - kbase;  // keys [0, lim] of this half-row are visible
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (c * 16 + e > lim) s[c][e] = __float_as_uint(-INFINITY);
+            mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(s[c][e]));
           }
-          mx[e & 7] = fmaxf(mx[e & 7], x);
-        }
+      }
       red[half * TQ + r] = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                  fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       pair_sync(quad);
