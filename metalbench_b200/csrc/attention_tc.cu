@@ -32,6 +32,8 @@
 // TMEM: S0 (128 cols) | S1 (128) | O (128) of a 512-column allocation.
 // Every mbarrier wait is bounded (common.cuh) and reports through the device
 // status word; the teardown drains the MMA pipe and in-flight copies.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -64,6 +66,12 @@ struct AttnTcParams {
   float scale_log2;
   uint16_t* out;
   int ldo;
+  // split-KV (non-causal only): CTA split sp handles key tiles
+  // [sp*tiles_per_split, +tiles_per_split) and writes its unnormalised O,
+  // running max and row sum per row to part_o / part_ml instead of out
+  int splits, tiles_per_split, Hq;
+  float* part_o;   // [B][Hq][S][splits][128]
+  float* part_ml;  // [B][Hq][S][splits][2]
 };
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -124,13 +132,16 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
   float* red = reinterpret_cast<float*>(base + OFF_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.n_qt - 1 - (int)blockIdx.x;  // longest causal tiles first
+  const int qt = p.n_qt - 1 - (int)blockIdx.x / p.splits;  // longest causal tiles first
+  const int sp = (int)blockIdx.x % p.splits;
   const int h = blockIdx.y, b = blockIdx.z, kvh = h / p.G;
   const int p0 = p.start_pos[b], L = p.kv_len[b];
   const int q_first = qt * TQ;
   int kend = L;
   if (p.causal) kend = min(L, p0 + min(p.S - 1, q_first + TQ - 1) + 1);
-  const int n_tiles = kend > 0 ? (kend + TK - 1) / TK : 0;
+  const int tiles_all = kend > 0 ? (kend + TK - 1) / TK : 0;
+  const int jbase = sp * p.tiles_per_split;  // first key tile of this CTA
+  const int n_tiles = max(0, min(tiles_all, jbase + p.tiles_per_split) - jbase);
   const int valid_pages = (L + PGK - 1) / PGK;
 
   if (threadIdx.x == 0) {
@@ -171,7 +182,7 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
     __syncwarp();
     // one key tile (up to two pages) of the K or V cache into slot `dst`
     auto load_tile = [&](int j, const CUtensorMap* map, uint8_t* dst, uint64_t* bar) {
-      const int pg0 = 2 * j;
+      const int pg0 = 2 * (jbase + j);
       const int npg = min(2, valid_pages - pg0);
       mbd::mbar_expect_tx(bar, (uint32_t)npg * 2 * HALF_PAGE);
       for (int pi = 0; pi < npg; ++pi) {
@@ -213,7 +224,7 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
     // partial page) must be finite: P is 0 there, but 0 * NaN is not.
     if (ok && n_tiles > 0) {
       const int j = n_tiles - 1, st = j & 1;
-      const int rows_valid = min(TK, L - TK * j);
+      const int rows_valid = min(TK, L - TK * (jbase + j));
       if (rows_valid < TK) {
         ok = __all_sync(0xffffffffu, mbd::mbar_wait(&vfull[st], (j >> 1) & 1, status,
                                                     MB_DEV_TIMEOUT_TMA, abort_flag));
@@ -332,7 +343,7 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
           for (int e = 0; e < 16; ++e) s[c][e] = 0u;
       }
       // mask in place; maximum of this half-row in 8 independent chains
-      const int kbase = j * TK + c0;
+      const int kbase = (jbase + j) * TK + c0;
       int kmax = L - 1;  // last key this row may see
       if (p.causal) kmax = min(kmax, qpos);
       const bool full = kbase + 63 <= kmax;
@@ -423,9 +434,31 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
     red[half * TQ + r] = l;
     pair_sync(quad);
     const float lt = red[r] + red[TQ + r];
-    if (fin) {
+    if (fin && p.splits > 1) {
+      // partial of this key split: unnormalised O, max (log2 units), row sum
+      mbd::tc_fence_after();
+      const int64_t prow = (((int64_t)b * p.Hq + h) * p.S + row) * p.splits + sp;
+      float4* dst = reinterpret_cast<float4*>(p.part_o + prow * DHT + c0);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[16];
+        mbd::tmem_ld16(tO + lane_off + c0 + c * 16, o);
+        mbd::tmem_ld_wait();
+        if (row < p.S)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[4 * c + e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                         __uint_as_float(o[4 * e + 2]),
+                                         __uint_as_float(o[4 * e + 3]));
+      }
+      if (row < p.S && half == 0) {
+        p.part_ml[prow * 2] = m;
+        p.part_ml[prow * 2 + 1] = lt;
+      }
+    } else if (fin) {
       mbd::tc_fence_after();
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const uint32_t keep = lt > 0.f ? 0xFFFFFFFFu : 0u;  // no visible key: O was never written
       uint4* dst =
           reinterpret_cast<uint4*>(p.out + ((int64_t)b * p.S + row) * p.ldo + h * DHT + c0);
 #pragma unroll 1
@@ -433,6 +466,8 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
         uint32_t o[16];
         mbd::tmem_ld16(tO + lane_off + c0 + c * 16, o);
         mbd::tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) o[e] &= keep;
         if (row < p.S) {
           uint4 w0, w1;
           w0.x = pack_bf16x2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
@@ -456,9 +491,41 @@ __global__ void __launch_bounds__(64 + NSOFT, 1)
   }
 }
 
+// out row = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s;
+// one 128-thread block per (sequence, head, query row), thread = dim
+__global__ void __launch_bounds__(128) attn_split_combine_kernel(
+    const float* __restrict__ part_o, const float* __restrict__ part_ml, int S, int Hq,
+    int splits, uint16_t* __restrict__ out, int ldo) {
+  const int64_t rid = blockIdx.x;  // (b * Hq + h) * S + row
+  const int row = (int)(rid % S);
+  const int h = (int)((rid / S) % Hq);
+  const int64_t b = rid / ((int64_t)S * Hq);
+  const float* ml = part_ml + rid * splits * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[2 * s]);
+  float acc = 0.f, lsum = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    if (ml[2 * s] == -INFINITY) continue;  // a split with no visible key: O never written
+    const float w = exp2f(ml[2 * s] - M);
+    lsum += w * ml[2 * s + 1];
+    acc += w * part_o[(rid * splits + s) * DHT + threadIdx.x];
+  }
+  const float v = lsum > 0.f ? acc / lsum : 0.f;
+  __nv_bfloat16 hv = __float2bfloat16_rn(v);
+  out[(b * S + row) * (int64_t)ldo + h * DHT + threadIdx.x] = *reinterpret_cast<uint16_t*>(&hv);
+}
+
 }  // namespace
 
 namespace mb {
+
+int attention_split_plan(int64_t B, int64_t S, int64_t Hq, int64_t kv_len) {
+  const int64_t ctas = B * Hq * ((S + TQ - 1) / TQ);
+  const int64_t tiles = (kv_len + TK - 1) / TK;
+  int64_t splits = num_sms() / std::max<int64_t>(ctas, 1);
+  splits = std::min<int64_t>(splits, tiles / 2);
+  return (int)std::max<int64_t>(splits, 1);
+}
 
 // false (and nothing launched) when the operands do not fit the TMA path
 bool attention_prefill_tc_ok(const uint16_t* q, int ldq, const uint16_t* k_cache,
@@ -471,7 +538,10 @@ bool attention_prefill_tc_ok(const uint16_t* q, int ldq, const uint16_t* k_cache
 int attention_prefill_tc(const uint16_t* q, int ldq, const uint16_t* k_cache,
                          const uint16_t* v_cache, const int* block_table, int max_pages,
                          const int* start_pos, const int* kv_len, int B, int S, int Hq, int Hkv,
-                         int causal, uint16_t* out, int ldo, cudaStream_t stream) {
+                         int causal, uint16_t* out, int ldo, cudaStream_t stream, int splits,
+                         int max_kv_len, float* part_o, float* part_ml) {
+  MB_REQUIRE(splits == 1 || (!causal && part_o && part_ml && max_kv_len > 0),
+             "attention: split-KV needs a non-causal call, max_kv_len and partial buffers");
   AttnTcParams p;
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
@@ -495,6 +565,12 @@ int attention_prefill_tc(const uint16_t* q, int ldq, const uint16_t* k_cache,
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)DHT);
   p.out = out;
   p.ldo = ldo;
+  p.splits = splits;
+  p.Hq = Hq;
+  p.part_o = part_o;
+  p.part_ml = part_ml;
+  p.tiles_per_split = splits == 1 ? (1 << 30)
+                                  : ((max_kv_len + TK - 1) / TK + splits - 1) / splits;
   int dev = 0;
   MB_CUDA(cudaGetDevice(&dev));
   static bool attr[64] = {};
@@ -503,9 +579,14 @@ int attention_prefill_tc(const uint16_t* q, int ldq, const uint16_t* k_cache,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     if (dev >= 0 && dev < 64) attr[dev] = true;
   }
-  dim3 grid((unsigned)p.n_qt, (unsigned)Hq, (unsigned)B);
+  dim3 grid((unsigned)(p.n_qt * splits), (unsigned)Hq, (unsigned)B);
   attn_prefill_tc_kernel<<<grid, 64 + NSOFT, SMEM_BYTES, stream>>>(p, device_status_ptr());
   MB_CUDA(cudaGetLastError());
+  if (splits > 1) {
+    attn_split_combine_kernel<<<(unsigned)((int64_t)B * Hq * S), 128, 0, stream>>>(
+        part_o, part_ml, S, Hq, splits, out, ldo);
+    MB_CUDA(cudaGetLastError());
+  }
   return MB_OK;
 }
 

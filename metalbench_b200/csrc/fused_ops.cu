@@ -12,6 +12,8 @@
 // with its row-scale and SwiGLU epilogues, and the paged attention kernel (a
 // contiguous [S, 128] K or V is a valid page sequence with an identity page
 // table).
+#include <algorithm>
+
 #include "decoder_epi.cuh"
 #include "gemm_launch.cuh"
 #include "kernels.h"
@@ -54,6 +56,91 @@ __global__ void add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16
       o[m] = gemm::pack_bf16(s0, s1);
     }
     yp[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// fused_add_rms_norm for D <= 8192: one 256-thread block per row, the row's
+// x + r kept in registers (at most 4 16-byte units of each per thread), so x
+// and r are read once.
+__global__ void __launch_bounds__(256) add_rms_norm_row_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ r, uint16_t* __restrict__ y,
+    int D, float eps) {
+  __shared__ float part[8];
+  const int64_t row = blockIdx.x;
+  const uint4* xp = reinterpret_cast<const uint4*>(x + row * D);
+  const uint4* rp = reinterpret_cast<const uint4*>(r + row * D);
+  const int units = D / 8;
+  float v[4][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int u = threadIdx.x + k * 256;
+    if (u < units) {
+      const uint4 a = xp[u], b = rp[u];
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        v[k][2 * m] = __uint_as_float(aw[m] << 16) + __uint_as_float(bw[m] << 16);
+        v[k][2 * m + 1] = __uint_as_float(aw[m] & 0xFFFF0000u) + __uint_as_float(bw[m] & 0xFFFF0000u);
+        ss += v[k][2 * m] * v[k][2 * m] + v[k][2 * m + 1] * v[k][2 * m + 1];
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += part[w];
+  const float rs = rsqrtf(tot / (float)D + eps);
+  uint4* yp = reinterpret_cast<uint4*>(y + row * D);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int u = threadIdx.x + k * 256;
+    if (u < units)
+      yp[u] = make_uint4(gemm::pack_bf16(v[k][0] * rs, v[k][1] * rs),
+                         gemm::pack_bf16(v[k][2] * rs, v[k][3] * rs),
+                         gemm::pack_bf16(v[k][4] * rs, v[k][5] * rs),
+                         gemm::pack_bf16(v[k][6] * rs, v[k][7] * rs));
+  }
+}
+
+// RoPE over the full width, 8 pairs (16 elements) per thread for D % 16 == 0:
+// omega_i from a per-block table, the angle s*omega_i reduced to [-pi, pi]
+// (two-term 2*pi, the angle itself being an fp32 product as in the
+// reference) and sin/cos on the SFU.
+__global__ void __launch_bounds__(256) rope_fast_kernel(const uint16_t* __restrict__ x,
+                                                        uint16_t* __restrict__ y, int S, int D,
+                                                        float neg_log2_base_over_half) {
+  extern __shared__ float omega[];  // [D/2]
+  const int half = D / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x)
+    omega[i] = exp2f(neg_log2_base_over_half * (float)i);
+  __syncthreads();
+  const int per_row = D / 16;
+  const int64_t n = (int64_t)S * per_row;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int s = (int)(t / per_row), i0 = (int)(t % per_row) * 8;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)s * D + 2 * i0);
+    uint4 in[2] = {src[0], src[1]};
+    uint4 out[2];
+    const uint32_t* iw = reinterpret_cast<const uint32_t*>(in);
+    uint32_t* ow = reinterpret_cast<uint32_t*>(out);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float a = (float)s * omega[i0 + k];
+      const float q = rintf(a * 0.15915494309189535f);
+      const float rr = fmaf(-q, -1.7484555e-7f, fmaf(-q, 6.28318548202514648f, a));
+      float sn, cs;
+      __sincosf(rr, &sn, &cs);
+      const float e0 = __uint_as_float(iw[k] << 16), e1 = __uint_as_float(iw[k] & 0xFFFF0000u);
+      ow[k] = gemm::pack_bf16(e0 * cs - e1 * sn, e0 * sn + e1 * cs);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(y + (int64_t)s * D + 2 * i0);
+    dst[0] = out[0];
+    dst[1] = out[1];
   }
 }
 
@@ -214,8 +301,12 @@ extern "C" int mb_fused_add_rms_norm_bf16(const uint16_t* x, const uint16_t* res
                                           void* stream) {
   MB_REQUIRE(M >= 0 && D > 0 && D % 8 == 0, "fused_add_rms_norm: D must be a multiple of 8");
   if (M == 0) return MB_OK;
-  add_rms_norm_kernel<<<(unsigned)((M + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, residual, y, (int)M, (int)D, eps);
+  if (D <= 8192 && M <= 0x7FFFFFFF)
+    add_rms_norm_row_kernel<<<(unsigned)M, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, residual, y, (int)D, eps);
+  else
+    add_rms_norm_kernel<<<(unsigned)((M + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, residual, y, (int)M, (int)D, eps);
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
@@ -225,8 +316,16 @@ extern "C" int mb_rope_bf16(const uint16_t* x, uint16_t* y, int64_t S, int64_t D
   MB_REQUIRE(S >= 0 && D > 0 && D % 2 == 0, "rope: D must be even");
   if (S == 0) return MB_OK;
   const int64_t n = S * (D / 2);
-  rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, y, (int)S, (int)D, -log2f(base) / (float)(D / 2));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D % 16 == 0 && D <= 16384) {
+    const int64_t units = S * (D / 16);
+    const int64_t blocks = std::min<int64_t>((units + 255) / 256, (int64_t)mb::num_sms() * 8);
+    rope_fast_kernel<<<(unsigned)blocks, 256, (size_t)(D / 2) * 4, s>>>(
+        x, y, (int)S, (int)D, -log2f(base) / (float)(D / 2));
+  } else {
+    rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, y, (int)S, (int)D,
+                                                           -log2f(base) / (float)(D / 2));
+  }
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
@@ -260,9 +359,28 @@ extern "C" int mb_swiglu_bf16(const uint16_t* x, const void* packed, uint16_t* o
                                                 static_cast<cudaStream_t>(stream), false, true);
 }
 
+namespace {
+struct SdpaWs {
+  int splits;
+  size_t tables, part_o, part_ml, total;
+};
+SdpaWs sdpa_ws(int64_t S) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  SdpaWs w;
+  // one head: ceil(S/128) query tiles alone leave most SMs idle, so the keys
+  // are split across CTAs (partials + a combine kernel)
+  w.splits = mb::attention_split_plan(1, S, 1, S);
+  w.tables = al((size_t)((S + 63) / 64 + 2) * 4);
+  w.part_o = w.splits > 1 ? al((size_t)S * w.splits * 128 * 4) : 0;
+  w.part_ml = w.splits > 1 ? al((size_t)S * w.splits * 2 * 4) : 0;
+  w.total = w.tables + w.part_o + w.part_ml;
+  return w;
+}
+}  // namespace
+
 extern "C" size_t mb_sdpa_workspace_bytes(int64_t S) {
   if (S <= 0) return 0;
-  return (size_t)(((S + 63) / 64 + 2) * 4 + 255) / 256 * 256;
+  return sdpa_ws(S).total;
 }
 
 extern "C" int mb_sdpa_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
@@ -271,16 +389,23 @@ extern "C" int mb_sdpa_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t
   MB_REQUIRE(d == 128, "sdpa: head dimension must be 128");
   MB_REQUIRE(S >= 0 && S <= (1 << 24), "sdpa: bad S");
   if (S == 0) return MB_OK;
-  MB_REQUIRE(workspace && workspace_bytes >= mb_sdpa_workspace_bytes(S),
-             "sdpa: workspace of %zu bytes required", mb_sdpa_workspace_bytes(S));
+  const SdpaWs wl = sdpa_ws(S);
+  MB_REQUIRE(workspace && workspace_bytes >= wl.total, "sdpa: workspace of %zu bytes required",
+             wl.total);
   const int pages = (int)((S + 63) / 64);
-  int* bt = static_cast<int*>(workspace);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  int* bt = reinterpret_cast<int*>(w);
   int* sp = bt + pages;
   int* kl = sp + 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   sdpa_tables_kernel<<<1, 256, 0, s>>>(bt, pages, sp, kl, (int)S);
   MB_CUDA(cudaGetLastError());
   // [S, 128] rows are pages of 64 keys for one kv head: an identity page table
+  if (wl.splits > 1 && mb::attention_prefill_tc_ok(Q, 128, K, V, O, 128))
+    return mb::attention_prefill_tc(Q, 128, K, V, bt, pages, sp, kl, 1, (int)S, 1, 1, 0, O, 128, s,
+                                    wl.splits, (int)S,
+                                    reinterpret_cast<float*>(w + wl.tables),
+                                    reinterpret_cast<float*>(w + wl.tables + wl.part_o));
   return mb_attention_prefill_bf16(Q, 128, K, V, bt, pages, sp, kl, 1, (int)S, 1, 1, 128, 0, O,
                                    128, stream);
 }

@@ -72,10 +72,15 @@ int gemm_bf16_ex(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, i
 // the operands.
 bool attention_prefill_tc_ok(const uint16_t* q, int ldq, const uint16_t* k_cache,
                              const uint16_t* v_cache, uint16_t* out, int ldo);
+// splits > 1 (non-causal): key range cut into `splits` parts per query tile,
+// partials in part_o [B][Hq][S][splits][128] / part_ml [..][2] (fp32), then
+// a combine kernel; attention_split_plan picks splits to fill the SMs.
 int attention_prefill_tc(const uint16_t* q, int ldq, const uint16_t* k_cache,
                          const uint16_t* v_cache, const int* block_table, int max_pages,
                          const int* start_pos, const int* kv_len, int B, int S, int Hq, int Hkv,
-                         int causal, uint16_t* out, int ldo, cudaStream_t stream);
+                         int causal, uint16_t* out, int ldo, cudaStream_t stream, int splits = 1,
+                         int max_kv_len = 0, float* part_o = nullptr, float* part_ml = nullptr);
+int attention_split_plan(int64_t B, int64_t S, int64_t Hq, int64_t kv_len);
 // decoder.cu helpers shared with fused_ops.cu
 int rownorm(const uint16_t* x, int M, int D, float eps, float* rstd, cudaStream_t s);
 int pack_tiled_weight(const uint16_t* in, int64_t ld_in, int K, const int* col_idx_dev, int Nout,
