@@ -115,6 +115,11 @@ int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return MB_OK;
 }
 
+bool pdl_enabled() {
+  static const bool on = getenv("MB_NO_PDL") == nullptr;
+  return on;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, CUtensorMapSwizzle swz) {

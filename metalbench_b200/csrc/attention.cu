@@ -36,6 +36,8 @@ __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 
 __global__ void attn_combine_kernel(const float* __restrict__ part_o,
                                     const float* __restrict__ part_ml, int splits, int G, int Hkv,
                                     uint16_t* __restrict__ out, int ldo) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   const int g = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
   const int64_t base = ((int64_t)b * Hkv + kvh) * splits;
   float M = -INFINITY;
@@ -292,6 +294,8 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
     const uint16_t* __restrict__ vc, const int* __restrict__ block_table, int max_pages,
     const int* __restrict__ kv_len, int Hkv, int G, int pages_per_split, float scale_log2,
     float* __restrict__ part_o, float* __restrict__ part_ml) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   extern __shared__ __align__(16) uint16_t sm[];
   uint16_t* Ks = sm;                                // [STAGES][64][KV_LD]
   uint16_t* Vs = sm + DEC_STAGES * PAGE * KV_LD;    // [STAGES][64][KV_LD]
@@ -515,12 +519,11 @@ extern "C" int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM));
     attr = true;
   }
-  attn_decode_mma_kernel<<<dim3(splits, Hkv, B), 128, DEC_SMEM, s>>>(
-      q, ldq, k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, pps, scale_log2, part_o,
-      part_ml);
-  MB_CUDA(cudaGetLastError());
-  attn_combine_kernel<<<dim3(G, Hkv, B), DH, 0, s>>>(part_o, part_ml, splits, G, Hkv, out, ldo);
-  MB_CUDA(cudaGetLastError());
+  MB_CUDA(mb::launch_pdl(attn_decode_mma_kernel, dim3(splits, Hkv, B), dim3(128), DEC_SMEM, s, q,
+                          ldq, k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, pps,
+                          scale_log2, part_o, part_ml));
+  MB_CUDA(mb::launch_pdl(attn_combine_kernel, dim3(G, Hkv, B), dim3(DH), 0, s,
+                          (const float*)part_o, (const float*)part_ml, splits, G, Hkv, out, ldo));
   return MB_OK;
 }
 

@@ -29,6 +29,28 @@ int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
 int num_sms();
 }  // namespace mb
 
+namespace mb {
+bool pdl_enabled();  // false when MB_NO_PDL is set
+// <<<grid, block, smem, stream>>> with programmatic stream serialisation, so
+// the kernel's prologue overlaps the tail of the previous kernel (see
+// pdl_wait); the kernel must call mbd::pdl_wait() before reading its inputs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+}  // namespace mb
+
 #define MB_CUDA(call)                                                      \
   do {                                                                     \
     cudaError_t _e = (call);                                               \
@@ -61,6 +83,19 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Programmatic dependent launch (PDL). A kernel launched with
+// mb::launch_pdl may start while the previous kernel of the stream is still
+// running: pdl_wait() blocks until that kernel has completed and its writes
+// are visible, so it must come before the first read of anything the previous
+// kernel wrote, and every CTA executes it (then the grid cannot complete
+// before its predecessor, which keeps dependencies transitive). pdl_trigger()
+// lets the next kernel start launching. Both are no-ops in a kernel launched
+// without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() {

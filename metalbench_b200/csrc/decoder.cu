@@ -32,6 +32,8 @@ namespace {
 // rstd[row] = 1 / sqrt(mean(x[row]^2) + eps); one warp per row, 16-byte loads.
 __global__ void rownorm_kernel(const uint16_t* __restrict__ x, int M, int D, float eps,
                                float* __restrict__ rstd) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -102,6 +104,8 @@ __device__ __forceinline__ void sum_slots(const float* __restrict__ part, const 
 // bf16 values it stored: the next RMSNorm without another pass.
 __global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                     gemm::EpiStore e, float* __restrict__ rstd_out, float eps) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   int row, col;
   if (rstd_out) {
     row = blockIdx.x;
@@ -150,6 +154,8 @@ __global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, 
 
 __global__ void reduce_qkv_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                   dec::QkvParams qp) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int chunks = N / RW;
   if (t >= (int64_t)M * chunks) return;
@@ -162,6 +168,8 @@ __global__ void reduce_qkv_kernel(const float* __restrict__ part, PartSum ps, in
 // N = 2*FF packed columns; thread per (row, 8 output features).
 __global__ void reduce_swiglu_kernel(const float* __restrict__ part, PartSum ps, int M, int N,
                                      dec::SwigluParams sp) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int chunks = sp.FF / RW;
   if (t >= (int64_t)M * chunks) return;
@@ -493,8 +501,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   int rc;
 
   // 1. rstd1
-  rownorm_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(x, (int)T, D, L.cfg.eps, rstd1);
-  MB_CUDA(cudaGetLastError());
+  MB_CUDA(mb::launch_pdl(rownorm_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s, x, (int)T,
+                          D, L.cfg.eps, rstd1));
 
   // 2. QKV + RoPE + KV-cache write
   dec::QkvParams qp;
@@ -512,7 +520,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(x, L.wqkv, part, T, Nqkv, D, p.ks_qkv, s, &ps);
     if (rc) return rc;
-    reduce_qkv_kernel<<<blocks_for(T * Nqkv / RW), 256, 0, s>>>(part, ps, (int)T, Nqkv, qp);
+    MB_CUDA(mb::launch_pdl(reduce_qkv_kernel, dim3(blocks_for(T * Nqkv / RW)), dim3(256), 0, s,
+                            part, ps, (int)T, Nqkv, qp));
   } else {
     dec::EpiQKV<256> e;
     e.M = (int)T;
@@ -548,12 +557,12 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s, &ps);
     if (rc) return rc;
     if (L.world == 1 && D / RW <= 1024) {  // the reduce also yields rstd2 (one CTA per row)
-      reduce_store_kernel<<<(unsigned)T, D / RW, 0, s>>>(part, ps, (int)T, D, eo, rstd2,
-                                                         L.cfg.eps);
+      MB_CUDA(mb::launch_pdl(reduce_store_kernel, dim3((unsigned)T), dim3(D / RW), 0, s, part, ps,
+                              (int)T, D, eo, rstd2, L.cfg.eps));
       rstd2_done = true;
     } else {
-      reduce_store_kernel<<<blocks_for(T * D / RW), 256, 0, s>>>(part, ps, (int)T, D, eo, nullptr,
-                                                                 0.f);
+      MB_CUDA(mb::launch_pdl(reduce_store_kernel, dim3(blocks_for(T * D / RW)), dim3(256), 0, s,
+                              part, ps, (int)T, D, eo, (float*)nullptr, 0.f));
     }
   } else {
     Epi<256, EpiStore> e{};
@@ -569,8 +578,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
 
   // 5. rstd2 (unless the o-proj reduce produced it), 6. SwiGLU MLP up
   if (!rstd2_done) {
-    rownorm_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(x1, (int)T, D, L.cfg.eps, rstd2);
-    MB_CUDA(cudaGetLastError());
+    MB_CUDA(mb::launch_pdl(rownorm_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
+                            (const uint16_t*)x1, (int)T, D, L.cfg.eps, rstd2));
   }
   dec::SwigluParams sp;
   sp.M = (int)T;
@@ -581,8 +590,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(x1, L.wgu, part, T, 2 * L.FF, D, p.ks_gu, s, &ps);
     if (rc) return rc;
-    reduce_swiglu_kernel<<<blocks_for(T * L.FF / RW), 256, 0, s>>>(part, ps, (int)T, 2 * L.FF,
-                                                                    sp);
+    MB_CUDA(mb::launch_pdl(reduce_swiglu_kernel, dim3(blocks_for(T * L.FF / RW)), dim3(256), 0, s,
+                            part, ps, (int)T, 2 * L.FF, sp));
   } else {
     dec::EpiSwiGLU e;
     e.M = (int)T;
@@ -605,8 +614,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     PartSum ps;
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s, &ps);
     if (rc) return rc;
-    reduce_store_kernel<<<blocks_for(T * D / RW), 256, 0, s>>>(part, ps, (int)T, D, ed, nullptr,
-                                                               0.f);
+    MB_CUDA(mb::launch_pdl(reduce_store_kernel, dim3(blocks_for(T * D / RW)), dim3(256), 0, s,
+                            part, ps, (int)T, D, ed, (float*)nullptr, 0.f));
   } else {
     Epi<256, EpiStore> e{};
     static_cast<EpiStore&>(e) = ed;

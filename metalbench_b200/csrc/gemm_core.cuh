@@ -397,6 +397,9 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   mbd::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // set-up above overlaps the previous kernel when launched with PDL
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
 
   // The producer and MMA warps run their loops with all 32 lanes (waits on
   // every lane, agreed by a warp vote) and only lane 0 issues the TMA copies,

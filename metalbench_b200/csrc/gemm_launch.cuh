@@ -72,7 +72,8 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
     sc.sk_per = pl.per;
     grid = pl.ctas;
   }
-  kern<<<grid, 256, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
+  MB_CUDA(mb::launch_pdl(kern, dim3(grid), dim3(256), S::TOTAL, stream, p, epi, sc,
+                          mb::device_status_ptr()));
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
@@ -125,7 +126,8 @@ inline int launch_gemm_decode(const void* A, const void* B, const Epi& epi, int6
     MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
     attr = true;
   }
-  kern<<<pl.ctas, 256, S::TOTAL, stream>>>(p, epi, sc, mb::device_status_ptr());
+  MB_CUDA(mb::launch_pdl(kern, dim3(pl.ctas), dim3(256), S::TOTAL, stream, p, epi, sc,
+                          mb::device_status_ptr()));
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
