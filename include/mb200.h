@@ -96,7 +96,7 @@ typedef struct mb_device {
   int smem_per_block_optin;
 } mb_device;
 
-/* ---- lifecycle / manifest API (SURVEY boundary: main.mm replacement) ---- */
+/* ---- lifecycle / manifest API (replaces metal/scripts/main.mm) ---- */
 
 /* Select the device for this process. rank/world/nccl_id_path are used by the
  * tensor-parallel entry points (world > 1); pass 0/1/NULL for one GPU.
