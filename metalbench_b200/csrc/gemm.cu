@@ -71,27 +71,61 @@ __global__ void split_a_kernel(const float4* __restrict__ a, float4* __restrict_
   }
 }
 
-// B [K,N] -> Bt_hi, Bt_lo [N,K] (transposed so both GEMM operands are K-major),
-// 32x32 tiles through a padded shared tile; blockIdx.z = batch (strides K*N).
-__global__ void split_bt_kernel(const float* __restrict__ b, float* __restrict__ hi,
-                                float* __restrict__ lo, int64_t K, int64_t N) {
-  __shared__ float T[32][33];
+// B [K,N] -> Bt_hi, Bt_lo [N,K] (transposed so both GEMM operands are K-major);
+// blockIdx.z = batch (strides K*N). 64 x 64 tiles through a padded shared
+// tile: 16-byte loads along N and 16-byte stores along K when K and N are
+// multiples of 4 (else element by element).
+__global__ void __launch_bounds__(256) split_bt_kernel(const float* __restrict__ b,
+                                                       float* __restrict__ hi,
+                                                       float* __restrict__ lo, int64_t K,
+                                                       int64_t N) {
+  __shared__ float T[64][65];
   const int64_t z = blockIdx.z;
   b += z * K * N;
   hi += z * K * N;
   lo += z * K * N;
-  const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-  for (int r = ty; r < 32; r += 8)
-    if (k0 + r < K && n0 + tx < N) T[r][tx] = b[(k0 + r) * N + n0 + tx];
-  __syncthreads();
-  for (int r = ty; r < 32; r += 8)
-    if (n0 + r < N && k0 + tx < K) {
-      float h, l;
-      split_tf32(T[tx][r], h, l);
-      hi[(n0 + r) * K + k0 + tx] = h;
-      lo[(n0 + r) * K + k0 + tx] = l;
+  const int64_t k0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+  const bool vec = (K % 4 == 0) && (N % 4 == 0) && k0 + 64 <= K && n0 + 64 <= N;
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // 64 rows x 16 float4
+      const int idx = threadIdx.x + i * 256, r = idx >> 4, c4 = (idx & 15) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(b + (k0 + r) * N + n0 + c4);
+      T[r][c4] = v.x;
+      T[r][c4 + 1] = v.y;
+      T[r][c4 + 2] = v.z;
+      T[r][c4 + 3] = v.w;
     }
+  } else {
+    for (int idx = threadIdx.x; idx < 64 * 64; idx += 256) {
+      const int r = idx >> 6, c = idx & 63;
+      if (k0 + r < K && n0 + c < N) T[r][c] = b[(k0 + r) * N + n0 + c];
+    }
+  }
+  __syncthreads();
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // 64 output rows (n) x 16 float4 along k, 256 B per row
+      const int idx = threadIdx.x + i * 256, n = idx >> 4, k4 = (idx & 15) * 4;
+      float4 h, l;
+      split_tf32(T[k4][n], h.x, l.x);
+      split_tf32(T[k4 + 1][n], h.y, l.y);
+      split_tf32(T[k4 + 2][n], h.z, l.z);
+      split_tf32(T[k4 + 3][n], h.w, l.w);
+      *reinterpret_cast<float4*>(hi + (n0 + n) * K + k0 + k4) = h;
+      *reinterpret_cast<float4*>(lo + (n0 + n) * K + k0 + k4) = l;
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < 64 * 64; idx += 256) {
+      const int n = idx >> 6, k = idx & 63;
+      if (n0 + n < N && k0 + k < K) {
+        float h, l;
+        split_tf32(T[k][n], h, l);
+        hi[(n0 + n) * K + k0 + k] = h;
+        lo[(n0 + n) * K + k0 + k] = l;
+      }
+    }
+  }
 }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -117,7 +151,7 @@ int tf32x3_gemm(const float* A, const float* B, float* C, int64_t batch, int64_t
                                           reinterpret_cast<float4*>(a_hi),
                                           reinterpret_cast<float4*>(a_lo), batch * M * K / 4);
   MB_CUDA(cudaGetLastError());
-  dim3 g((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32), (unsigned)batch);
+  dim3 g((unsigned)((N + 63) / 64), (unsigned)((K + 63) / 64), (unsigned)batch);
   MB_REQUIRE(g.y <= 65535 && g.z <= 65535, "tf32x3: K or batch too large");
   split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
   MB_CUDA(cudaGetLastError());
