@@ -102,18 +102,20 @@ class DecoderLayer:
 
     def forward(self, x: torch.Tensor, cache: PagedKVCache, start_pos: torch.Tensor,
                 causal: bool = True, out: torch.Tensor | None = None,
-                max_kv_len: int | None = None) -> torch.Tensor:
+                max_kv_len: int | None = None, kv_len: torch.Tensor | None = None) -> torch.Tensor:
         """x: [B, S, D] bf16 (or [S, D] for B = 1); start_pos: int32 [B] on the device.
 
         The new tokens' keys/values are appended at start_pos[b].. and attention
-        reads positions 0..start_pos[b]+S-1."""
+        reads positions 0..start_pos[b]+S-1. kv_len (= start_pos + S, int32 on
+        the device) may be passed in when several layers share it."""
         squeeze = x.dim() == 2
         X = x.unsqueeze(0) if squeeze else x
         ops._cuda(X, "DecoderLayer.forward(x)", (torch.bfloat16,))
         B, S, D = X.shape
         if start_pos.dtype != torch.int32 or not start_pos.is_cuda or start_pos.numel() != B:
             raise ValueError("start_pos must be an int32 CUDA tensor with one entry per sequence")
-        kv_len = (start_pos + S).contiguous()
+        if kv_len is None:
+            kv_len = (start_pos + S).contiguous()
         if max_kv_len is None:
             max_kv_len = int(kv_len.max().item())
         if out is None:

@@ -77,8 +77,12 @@ class DecoderStack:
 
     def forward(self, x: torch.Tensor, start_pos: torch.Tensor, causal: bool = True,
                 kv_len_max: int | None = None) -> torch.Tensor:
+        # one kv_len for all layers: no extra kernel between two layers' launches
+        S = x.shape[-2] if x.dim() == 3 else x.shape[0]
+        self._kv_len = (start_pos + S).contiguous()
         for layer, cache in zip(self.layers, self.caches):
-            x = layer(x, cache, start_pos, causal=causal, max_kv_len=kv_len_max)
+            x = layer(x, cache, start_pos, causal=causal, max_kv_len=kv_len_max,
+                      kv_len=self._kv_len)
         return x
 
     # ---- decode step in a CUDA graph ---------------------------------------
