@@ -191,11 +191,24 @@ int dtype_tag(const std::string& d) {
 }
 
 // The reference's Metal function names of the hot-path kernels -> libmb200.
+// (The standard- and full-set kernels take bf16 buffers: manifests for them
+// set "dtype": "bf16", an extension of the reference's f32/f16/i32/u32.)
 const std::map<std::string, std::string> kFunctionToKernel = {
     {"sqr_matmul_f32", "sqr_mm"},
+    {"rect_matmul_f32", "sqr_mm"},
+    {"batch_matmul_f32", "batch_mm"},
     {"transpose_2d_f32", "transpose_2d"},
     {"conv2d_f32", "conv2d"},
     {"llama_decoder_layer_f32", "llama_decoder_layer"},
+    {"rms_norm_linear_f32", "rms_norm_linear"},
+    {"fused_add_rms_norm_f32", "fused_add_rms_norm"},
+    {"rope_embedding_f32", "rope_embedding"},
+    {"swiglu_f32", "swiglu"},
+    {"fused_qkv_projection_f32", "gemm_bf16"},
+    {"scaled_dot_product_f32", "scaled_dot_product"},
+    {"llama_attention_f32", "llama_attention"},
+    {"mha_attention_f32", "mha_attention"},
+    {"transformer_block_f32", "transformer_block"},
 };
 
 std::string json_escape(const char* s) {
