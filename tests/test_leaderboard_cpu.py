@@ -55,3 +55,32 @@ def test_kernels_for_maps_changes_to_registry_names():
 
 def test_certify_script_parses():
     assert subprocess.run(["bash", "-n", str(REPO / "certify")]).returncode == 0
+
+
+def test_certify_parses_the_harness_report(capsys):
+    """certify extracts time, speedup, GFLOPS and GB/s from the report lines
+    with awk field positions (the reference's certify:66-71); pin them on a
+    report printed from a synthetic result."""
+    from metalbench_b200 import harness as Hm
+    res = {"task": "sqr_mm", "correct": True, "solo": None, "reference_impl": "mlx-compat",
+           "reference_cpu_threads": 16, "tg_static_mem_bytes": 197752,
+           "pso_max_threads_per_tg": 256,
+           "chip": {"name": "NVIDIA B200", "type": "b200", "cpu_cores": 16, "gpu_cores": 148,
+                    "ram_bytes": 2e11},
+           "outputs": [{"max_err": 4.3e-4, "frac_within_tol": 1.0}],
+           "kernel_timing": {"median_ms": 0.115, "min_ms": 0.113, "mean_ms": 0.116, "iters": 200},
+           "reference_timing": {"median_ms": 12.0, "min_ms": 11.9, "mean_ms": 12.1, "iters": 5},
+           "metrics": {"speedup": 104.3, "gflops": 149389.1, "gbps": 437.7,
+                       "arith_intensity": 341.3, "stability": 0.99}}
+    Hm.print_report(res, "speed", 104.3)
+    out = capsys.readouterr().out
+    script = r"""
+      ms=$(awk '/^  kernel  /   { gsub(/ms/,"",$3); print $3; exit }' <<<"$OUT")
+      sp=$(awk '/^  speedup/    { gsub(/×/,"",$3); print $3; exit }' <<<"$OUT")
+      gf=$(awk '/^  compute/    { print $3; exit }' <<<"$OUT")
+      gb=$(awk '/^  bandwidth/  { print $3; exit }' <<<"$OUT")
+      grep -q "correctness : ✓ correct" <<<"$OUT" && echo "$ms $sp $gf $gb"
+    """
+    r = subprocess.run(["bash", "-c", script], env={"OUT": out, "PATH": "/usr/bin:/bin"},
+                       capture_output=True, text=True)
+    assert r.stdout.split() == ["0.115", "104.30", "149389.1", "437.7"], (r.stdout, out)
