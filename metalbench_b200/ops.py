@@ -171,6 +171,8 @@ def rms_norm_linear(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torc
     init(x.device.index)
     M, K = x.shape
     N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"rms_norm_linear: w must be [N, {K}], got {tuple(w.shape)}")
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     nb = _lib.lib().mb_rms_norm_linear_workspace_bytes(M)
     ws = _workspace(nb, x.device)
@@ -182,6 +184,8 @@ def rms_norm_linear(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torc
 def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
     _cuda(x, "fused_add_rms_norm(x)", (torch.bfloat16,))
     _cuda(residual, "fused_add_rms_norm(residual)", (torch.bfloat16,))
+    if residual.shape != x.shape:
+        raise ValueError("fused_add_rms_norm: x and residual shapes differ")
     init(x.device.index)
     y = torch.empty_like(x)
     _lib.call("mb_fused_add_rms_norm_bf16", x.data_ptr(), residual.data_ptr(), y.data_ptr(),
@@ -201,6 +205,8 @@ def rope(x: torch.Tensor, base: float = 10000.0) -> torch.Tensor:
 def swiglu_pack(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
     _cuda(w_gate, "swiglu_pack(w_gate)", (torch.bfloat16,))
     _cuda(w_up, "swiglu_pack(w_up)", (torch.bfloat16,))
+    if w_up.shape != w_gate.shape:
+        raise ValueError("swiglu_pack: w_gate and w_up shapes differ")
     init(w_gate.device.index)
     D, FF = w_gate.shape
     packed = torch.empty(_lib.lib().mb_swiglu_packed_bytes(D, FF), dtype=torch.uint8,
@@ -215,6 +221,8 @@ def swiglu(x: torch.Tensor, packed: torch.Tensor, ffn: int) -> torch.Tensor:
     _cuda(x, "swiglu(x)", (torch.bfloat16,))
     init(x.device.index)
     M, D = x.shape
+    if packed.numel() < _lib.lib().mb_swiglu_packed_bytes(D, ffn):
+        raise ValueError("swiglu: packed weights are smaller than swiglu_pack makes for D, ffn")
     out = torch.empty((M, ffn), dtype=torch.bfloat16, device=x.device)
     _lib.call("mb_swiglu_bf16", x.data_ptr(), packed.data_ptr(), out.data_ptr(), M, D, ffn,
               _stream())
@@ -225,6 +233,8 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """softmax(q k^T / sqrt(128)) v for one head, [S, 128] bf16."""
     for n, t in (("q", q), ("k", k), ("v", v)):
         _cuda(t, f"sdpa({n})", (torch.bfloat16,))
+    if not (q.shape == k.shape == v.shape) or q.dim() != 2:
+        raise ValueError("sdpa: q, k, v must all be [S, 128]")
     init(q.device.index)
     S = q.shape[0]
     o = torch.empty_like(q)
