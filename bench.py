@@ -42,6 +42,23 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
+def traffic_key(workload: str, world: int) -> str:
+    """Profiles record traffic per workload and GPU count: the dominant
+    kernel's per-launch bytes change with the tensor-parallel degree."""
+    return workload if world == 1 else f"{workload}@n{world}"
+
+
+def blas_threads(threads: int):
+    """Size numpy's BLAS pool explicitly (torchrun exports OMP_NUM_THREADS=1,
+    which would otherwise leave the CPU baseline on one core at N>1) and
+    return (context manager, threads actually in use)."""
+    import numpy  # noqa: F401  (loads the BLAS library the limit applies to)
+    from threadpoolctl import threadpool_info, threadpool_limits
+    ctx = threadpool_limits(limits=threads, user_api="blas")
+    got = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+    return ctx, (max(got) if got else threads)
+
+
 def profile_traffic(key: str):
     """dram bytes per launch recorded by an ncu capture summary under profiles/
     (a line ``traffic_bytes_per_launch[<key>]: <int>``), or None."""
@@ -438,11 +455,13 @@ def run_reference(args, wl):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
+    ctx, threads = blas_threads(threads)
     vals, sample = [], ""
-    for i in range(args.warmup + args.steps):  # each step is a bounded sample
-        v, sample = wl.cpu_sample(threads)
-        if i >= args.warmup:
-            vals.append(v)
+    with ctx:
+        for i in range(args.warmup + args.steps):  # each step is a bounded sample
+            v, sample = wl.cpu_sample(threads)
+            if i >= args.warmup:
+                vals.append(v)
     value = statistics.median(vals)
     line = {"metric": wl.metric, "value": value, "unit": wl.unit, "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -564,8 +583,9 @@ def main(argv=None):
         return 0
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        v, sample = wl.cpu_sample(threads)
+        ctx, threads = blas_threads(os.cpu_count() or 1)
+        with ctx:
+            v, sample = wl.cpu_sample(threads)
         cpu = {"value": v, "unit": wl.unit, "cores": threads, "kind": "port", "sample": sample}
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
@@ -575,7 +595,7 @@ def main(argv=None):
         "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": r_unit,
                      "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)"
                      if peak_kind == "measured" else "fallback",
-                     "traffic": profile_traffic(wl.name), "launch_ms": launch_ms,
+                     "traffic": profile_traffic(traffic_key(wl.name, world)), "launch_ms": launch_ms,
                      "kernel": getattr(wl, "dominant", wl.name)},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,

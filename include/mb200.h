@@ -115,8 +115,11 @@ const char* mb_kernel_names(void);
 int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const mb_scalar* scalars, int nsc,
            const char* config_json, int warmup, int iters, mb_timing* out);
 
-/* Status word that bounded device waits write on timeout; 0 = clean. Reading
- * it synchronises the device. mb_clear_device_status resets it. */
+/* Status word that bounded device waits write on timeout; 0 = clean. There is
+ * one word per device; both calls act on the current device. Reading it
+ * synchronises the device. mb_clear_device_status resets it. The value also
+ * includes the word mb_sqr_mm_f32_noalloc falls back to on a device that has
+ * no shared word yet. */
 int mb_device_status(uint32_t* out);
 int mb_clear_device_status(void);
 
@@ -310,7 +313,13 @@ int mb_batch_mm_f32(const float* A, const float* B, float* C, int64_t batch, int
  *    cudaGetSymbolAddress, so make it before any stream capture.
  *  - All calls share the one array: calls that overlap on the GPU (different
  *    streams, or other processes' threads on the same context) race and give
- *    wrong results. Serialise them, e.g. on one stream. */
+ *    wrong results. Serialise them, e.g. on one stream.
+ *  - Like the other device-pointer entry points it returns once the work is
+ *    queued. A bounded device wait that runs out is reported afterwards by
+ *    mb_device_status (non-zero) and cleared by mb_clear_device_status: the
+ *    device's shared status word is used when it exists (after mb_init or any
+ *    allocating entry point), else a word compiled into the library beside
+ *    the scratch array, which mb_device_status also reads. */
 size_t mb_sqr_mm_f32_noalloc_max_workspace_bytes(void);
 int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N,
                           int64_t K, void* stream);

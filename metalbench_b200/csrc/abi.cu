@@ -19,6 +19,8 @@
 #include <cstdlib>
 #include <functional>
 #include <map>
+#include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -29,7 +31,19 @@ namespace mb {
 
 static thread_local std::string g_last_error;
 static int g_device = -1;
-static uint32_t* g_status = nullptr;  // device status word (bounded waits)
+
+// One device status word per GPU (bounded waits write into it), allocated on
+// first use with that device current, so a kernel is never handed another
+// GPU's word.
+constexpr int kMaxDevices = 64;
+static uint32_t* g_status[kMaxDevices] = {};
+static std::mutex g_status_mu;
+
+static int current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  return dev;
+}
 
 void set_error(const char* fmt, ...) {
   char buf[1024];
@@ -46,17 +60,30 @@ int cuda_fail(cudaError_t e, const char* what, const char* file, int line) {
 }
 
 uint32_t* device_status_ptr() {
-  if (!g_status) {
-    if (cudaMalloc(&g_status, sizeof(uint32_t)) != cudaSuccess) return nullptr;
-    cudaMemset(g_status, 0, sizeof(uint32_t));
+  const int dev = current_device();
+  if (dev < 0) return nullptr;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!g_status[dev]) {
+    uint32_t* p = nullptr;
+    if (cudaMalloc(&p, sizeof(uint32_t)) != cudaSuccess) return nullptr;
+    cudaMemset(p, 0, sizeof(uint32_t));
+    g_status[dev] = p;
   }
-  return g_status;
+  return g_status[dev];
+}
+
+uint32_t* existing_device_status_ptr() {
+  const int dev = current_device();
+  if (dev < 0) return nullptr;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  return g_status[dev];
 }
 
 int check_device_status(cudaStream_t stream) {
-  if (!g_status) return MB_OK;
+  uint32_t* st = existing_device_status_ptr();
+  if (!st) return MB_OK;
   uint32_t v = 0;
-  MB_CUDA(cudaMemcpyAsync(&v, g_status, sizeof(v), cudaMemcpyDeviceToHost, stream));
+  MB_CUDA(cudaMemcpyAsync(&v, st, sizeof(v), cudaMemcpyDeviceToHost, stream));
   MB_CUDA(cudaStreamSynchronize(stream));
   if (v) {
     set_error("a bounded device wait timed out (status 0x%x)", v);
@@ -66,13 +93,26 @@ int check_device_status(cudaStream_t stream) {
 }
 
 int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  static int n[kMaxDevices] = {};
+  const int dev = current_device();
+  if (dev < 0) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v;  // an int store: racing threads write the same value
   }
-  return n;
+  return n[dev];
+}
+
+int ensure_smem_attr(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({fn, dev})) return MB_OK;
+  MB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({fn, dev});
+  return MB_OK;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -230,9 +270,17 @@ extern "C" int mb_init(int device, int rank, int world, const char* nccl_id_path
 
 extern "C" void mb_shutdown(void) {
   tp_shutdown();
-  if (g_status) {
-    cudaFree(g_status);
-    g_status = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_status_mu);
+    int cur = -1;
+    cudaGetDevice(&cur);
+    for (int d = 0; d < kMaxDevices; ++d) {
+      if (!g_status[d]) continue;
+      cudaSetDevice(d);
+      cudaFree(g_status[d]);
+      g_status[d] = nullptr;
+    }
+    if (cur >= 0) cudaSetDevice(cur);
   }
   g_device = -1;
 }
@@ -278,16 +326,24 @@ extern "C" const char* mb_kernel_names(void) {
 extern "C" int mb_device_status(uint32_t* out) {
   MB_REQUIRE(out != nullptr, "mb_device_status: null output");
   *out = 0;
-  if (!g_status) return MB_OK;
-  MB_CUDA(cudaDeviceSynchronize());
-  MB_CUDA(cudaMemcpy(out, g_status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  uint32_t* st = existing_device_status_ptr();
+  uint32_t v = 0;
+  if (st) {
+    MB_CUDA(cudaDeviceSynchronize());
+    MB_CUDA(cudaMemcpy(&v, st, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  }
+  uint32_t w = 0;
+  const int rc = noalloc_status(&w, false);
+  if (rc) return rc;
+  *out = v | w;
   return MB_OK;
 }
 
 extern "C" int mb_clear_device_status(void) {
-  if (!g_status) return MB_OK;
-  MB_CUDA(cudaMemset(g_status, 0, sizeof(uint32_t)));
-  return MB_OK;
+  uint32_t* st = existing_device_status_ptr();
+  if (st) MB_CUDA(cudaMemset(st, 0, sizeof(uint32_t)));
+  uint32_t w = 0;
+  return noalloc_status(&w, true);
 }
 
 namespace {
@@ -295,6 +351,18 @@ struct DevAlloc {
   std::vector<void*> ptrs;
   ~DevAlloc() {
     for (void* p : ptrs) cudaFree(p);
+  }
+};
+// Every event mb_run creates, destroyed on every return path.
+struct EventPool {
+  std::vector<cudaEvent_t> evs;
+  cudaError_t make(cudaEvent_t* e) {
+    const cudaError_t r = cudaEventCreate(e);
+    if (r == cudaSuccess) evs.push_back(*e);
+    return r;
+  }
+  ~EventPool() {
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
   }
 };
 }  // namespace
@@ -323,9 +391,10 @@ extern "C" int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const m
     ~StreamGuard() { cudaStreamDestroy(s); }
   } sg{stream};
   DevAlloc alloc;
+  EventPool evp;
   cudaEvent_t h0, h1;
-  MB_CUDA(cudaEventCreate(&h0));
-  MB_CUDA(cudaEventCreate(&h1));
+  MB_CUDA(evp.make(&h0));
+  MB_CUDA(evp.make(&h1));
 
   // Bind buffers: host inputs are uploaded, host outputs get device storage.
   MB_CUDA(cudaEventRecord(h0, stream));
@@ -376,7 +445,7 @@ extern "C" int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const m
   if (rc) return rc;
 
   std::vector<cudaEvent_t> ev(2 * (size_t)iters);
-  for (auto& e : ev) MB_CUDA(cudaEventCreate(&e));
+  for (auto& e : ev) MB_CUDA(evp.make(&e));
   for (int i = 0; i < iters; ++i) {
     if (flush) MB_CUDA(cudaMemsetAsync(flush, i & 0xff, flush_bytes, stream));
     MB_CUDA(cudaEventRecord(ev[2 * i], stream));
@@ -393,7 +462,6 @@ extern "C" int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const m
     MB_CUDA(cudaEventElapsedTime(&ms, ev[2 * i], ev[2 * i + 1]));
     times[i] = ms;
   }
-  for (auto& e : ev) cudaEventDestroy(e);
   if (st.finish) {
     rc = st.finish(stream);
     if (rc) return rc;
@@ -409,8 +477,6 @@ extern "C" int mb_run(const char* kernel, const mb_buf* bufs, int nbufs, const m
   MB_CUDA(cudaEventSynchronize(h1));
   float d2h = 0;
   MB_CUDA(cudaEventElapsedTime(&d2h, h0, h1));
-  cudaEventDestroy(h0);
-  cudaEventDestroy(h1);
 
   std::sort(times.begin(), times.end());
   double sum = 0;

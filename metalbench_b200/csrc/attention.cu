@@ -513,12 +513,8 @@ extern "C" int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16
   float* part_ml = part_o + (size_t)B * Hq * splits * DH;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)DH);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  static bool attr = false;
-  if (!attr) {
-    MB_CUDA(cudaFuncSetAttribute(attn_decode_mma_kernel,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM));
-    attr = true;
-  }
+  int rc = mb::ensure_smem_attr(reinterpret_cast<const void*>(attn_decode_mma_kernel), DEC_SMEM);
+  if (rc) return rc;
   MB_CUDA(mb::launch_pdl(attn_decode_mma_kernel, dim3(splits, Hkv, B), dim3(128), DEC_SMEM, s, q,
                           ldq, k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, pps,
                           scale_log2, part_o, part_ml));
@@ -545,14 +541,9 @@ extern "C" int mb_attention_prefill_bf16(const uint16_t* q, int ldq, const uint1
   const int smem = 4 * PAGE * KV_LD * 2;
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)DH);
   dim3 grid((S + 63) / 64, Hq, B);
-  static bool attr = false;
-  if (!attr) {
-    MB_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    MB_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<false>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  int arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(attn_prefill_kernel<true>), smem);
+  if (!arc) arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(attn_prefill_kernel<false>), smem);
+  if (arc) return arc;
   if (causal)
     attn_prefill_kernel<true><<<grid, 128, smem, s>>>(q, ldq, k_cache, v_cache, block_table,
                                                        max_pages, start_pos, kv_len, S, Hkv,

@@ -571,13 +571,10 @@ int attention_prefill_tc(const uint16_t* q, int ldq, const uint16_t* k_cache,
   p.part_ml = part_ml;
   p.tiles_per_split = splits == 1 ? (1 << 30)
                                   : ((max_kv_len + TK - 1) / TK + splits - 1) / splits;
-  int dev = 0;
-  MB_CUDA(cudaGetDevice(&dev));
-  static bool attr[64] = {};
-  if (dev < 0 || dev >= 64 || !attr[dev]) {
-    MB_CUDA(cudaFuncSetAttribute(attn_prefill_tc_kernel,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    if (dev >= 0 && dev < 64) attr[dev] = true;
+  {
+    const int arc =
+        mb::ensure_smem_attr(reinterpret_cast<const void*>(attn_prefill_tc_kernel), SMEM_BYTES);
+    if (arc) return arc;
   }
   dim3 grid((unsigned)(p.n_qt * splits), (unsigned)Hq, (unsigned)B);
   attn_prefill_tc_kernel<<<grid, 64 + NSOFT, SMEM_BYTES, stream>>>(p, device_status_ptr());

@@ -18,7 +18,14 @@ int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
 // Device-side status word: kernels that give up a bounded wait write a code
 // here; the host reads it after the launch (mb_check_device_status).
 uint32_t* device_status_ptr();
+// The current device's status word if it was allocated already, else null
+// (never allocates).
+uint32_t* existing_device_status_ptr();
 int check_device_status(cudaStream_t stream);
+// The status word mb_sqr_mm_f32_noalloc uses on the current device before
+// that device has a shared one: read into *out (0 if never set up), cleared
+// when `clear` is set. Allocates nothing.
+int noalloc_status(uint32_t* out, bool clear);
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
@@ -27,6 +34,9 @@ int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
                  const uint64_t* dims, const uint64_t* strides_bytes /*rank-1*/,
                  const uint32_t* box, CUtensorMapSwizzle swz);
 int num_sms();
+// Opt `fn` into `bytes` of dynamic shared memory on the current device, once
+// per (function, device); safe to call from several host threads.
+int ensure_smem_attr(const void* fn, int bytes);
 }  // namespace mb
 
 namespace mb {

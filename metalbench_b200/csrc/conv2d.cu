@@ -252,10 +252,9 @@ int launch_conv(const uint16_t* x, const uint16_t* w, uint16_t* y, const ConvGeo
   e.g = g;
   e.y = y;
   auto kern = gemm_kernel<BN, STAGES, P, E>;
-  static bool attr = false;
-  if (!attr) {
-    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-    attr = true;
+  {
+    const int arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(kern), S::TOTAL);
+    if (arc) return arc;
   }
   const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
   kern<<<grid, 256, S::TOTAL, stream>>>(p, e, sc, mb::device_status_ptr());
@@ -307,10 +306,9 @@ int launch_conv_res(const uint16_t* x, const uint16_t* w, uint16_t* y, const Con
   e.fd_tw = p.fd_tw;
   e.y = y;
   auto kern = gemm_kernel<BN, STAGES, P, E>;
-  static bool attr = false;
-  if (!attr) {
-    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-    attr = true;
+  {
+    const int arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(kern), S::TOTAL);
+    if (arc) return arc;
   }
   const int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
   kern<<<grid, 256, S::TOTAL, stream>>>(p, e, sc, mb::device_status_ptr());

@@ -6,6 +6,8 @@
 // matmul helper mlx/kernels/common/registry.py:44-61 (row-major A [M,K],
 // B [K,N], C [M,N]); the Metal kernel metal/kernels/common/sqr_mm.metal:19-111
 // is a 64x64x16 simdgroup-MMA tile loop that this replaces.
+#include <mutex>
+
 #include "gemm_core.cuh"
 #include "gemm_epi.cuh"
 #include "gemm_launch.cuh"
@@ -185,12 +187,9 @@ int tf32x3_gemm(const float* A, const float* B, float* C, int64_t batch, int64_t
   sc.ksplit = 1;
   sc.kb_per_split = sc.kblocks;
   auto kern = gemm_kernel<128, 3, P, decltype(e), kTf32PromoteBlocks>;
-  int dev = 0;
-  MB_CUDA(cudaGetDevice(&dev));
-  static bool attr[64] = {};  // the attribute is set per device
-  if (dev < 0 || dev >= 64 || !attr[dev]) {
-    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-    if (dev >= 0 && dev < 64) attr[dev] = true;
+  {
+    const int arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(kern), S::TOTAL);
+    if (arc) return arc;
   }
   const int grid = sc.total() < sms ? sc.total() : sms;
   kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, status);
@@ -284,9 +283,11 @@ struct NoAllocSlot {
 };
 constexpr int kMaxDevices = 64;
 NoAllocSlot g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mu;
 
-int noalloc_setup(int dev, NoAllocSlot** out) {
+int noalloc_setup(int dev, NoAllocSlot* out) {
   MB_REQUIRE(dev >= 0 && dev < kMaxDevices, "mb_sqr_mm_f32_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
   NoAllocSlot& s = g_noalloc[dev];
   if (!s.scratch) {
     void* p = nullptr;
@@ -296,11 +297,29 @@ int noalloc_setup(int dev, NoAllocSlot** out) {
     s.status = static_cast<uint32_t*>(q);
     s.scratch = p;
   }
-  *out = &s;
+  *out = s;
   return MB_OK;
 }
 
 }  // namespace
+
+namespace mb {
+int noalloc_status(uint32_t* out, bool clear) {
+  *out = 0;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MB_OK;
+  uint32_t* st = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    st = g_noalloc[dev].status;
+  }
+  if (!st) return MB_OK;  // the entry point never ran on this device
+  MB_CUDA(cudaDeviceSynchronize());
+  MB_CUDA(cudaMemcpy(out, st, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  if (clear) MB_CUDA(cudaMemset(st, 0, sizeof(uint32_t)));
+  return MB_OK;
+}
+}  // namespace mb
 
 extern "C" size_t mb_sqr_mm_f32_noalloc_max_workspace_bytes(void) { return kNoAllocScratchBytes; }
 
@@ -318,12 +337,17 @@ extern "C" int mb_sqr_mm_f32_noalloc(const float* A, const float* B, float* C, i
              (long long)M, (long long)N, (long long)K, need, kNoAllocScratchBytes);
   int dev = 0;
   MB_CUDA(cudaGetDevice(&dev));
-  NoAllocSlot* slot = nullptr;
+  NoAllocSlot slot;
   int rc = noalloc_setup(dev, &slot);
   if (rc) return rc;
+  // Bounded-wait timeouts go to the device's shared status word when mb_init
+  // (or any other entry point) created it, else to the array-backed word;
+  // mb_device_status reports both, mb_clear_device_status clears both.
+  uint32_t* status = mb::existing_device_status_ptr();
+  if (!status) status = slot.status;
 
   // The split prepass overwrites every scratch byte the GEMM reads, so nothing
   // has to be cleared first.
-  return tf32x3_gemm(A, B, C, 1, M, N, K, static_cast<uint8_t*>(slot->scratch), slot->status,
+  return tf32x3_gemm(A, B, C, 1, M, N, K, static_cast<uint8_t*>(slot.scratch), status,
                      static_cast<cudaStream_t>(stream));
 }

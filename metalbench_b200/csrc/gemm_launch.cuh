@@ -58,10 +58,9 @@ inline int launch_gemm(const void* A, const void* B, const Epi& epi, int64_t M, 
   // no empty trailing split: every split owns at least one k-block
   sc.ksplit = (sc.kblocks + sc.kb_per_split - 1) / sc.kb_per_split;
   auto kern = gemm_kernel<BN, STAGES, P, Epi>;
-  static bool attr = false;  // one instantiation = one static
-  if (!attr) {
-    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-    attr = true;
+  {
+    const int arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(kern), S::TOTAL);
+    if (arc) return arc;
   }
   int grid = sc.total() < mb::num_sms() ? sc.total() : mb::num_sms();
   if (streamk) {
@@ -121,10 +120,9 @@ inline int launch_gemm_decode(const void* A, const void* B, const Epi& epi, int6
   sc.streamk = 1;
   sc.sk_per = pl.per;
   auto kern = gemm_kernel<BN, STAGES, P, Epi>;
-  static bool attr = false;
-  if (!attr) {
-    MB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
-    attr = true;
+  {
+    const int arc = mb::ensure_smem_attr(reinterpret_cast<const void*>(kern), S::TOTAL);
+    if (arc) return arc;
   }
   MB_CUDA(mb::launch_pdl(kern, dim3(pl.ctas), dim3(256), S::TOTAL, stream, p, epi, sc,
                           mb::device_status_ptr()));

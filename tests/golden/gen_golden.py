@@ -16,6 +16,7 @@ nothing at test time reads the reference checkout.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import importlib.util
 import sys
@@ -61,8 +62,11 @@ def _load_hook(ref: Path, kset: str, name: str):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=str(Path("/", "root", "reference")))
+    ap.add_argument("--reference", default=os.environ.get("MB_REFERENCE_TREE"),
+                    help="checkout of the reference repository (or set MB_REFERENCE_TREE)")
     args = ap.parse_args(argv)
+    if not args.reference:
+        ap.error("--reference (or MB_REFERENCE_TREE) is required")
     ref = Path(args.reference)
     try:
         import mlx.core  # noqa: F401

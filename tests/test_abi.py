@@ -54,3 +54,14 @@ def test_run_without_init_reports_not_init(lib):
     from metalbench_b200 import _lib
     rc = lib.mb_run(b"transpose_2d", None, 0, None, 0, None, 0, 1, None)
     assert rc == -6 and "mb_init" in _lib.last_error()
+
+
+def test_device_status_reader_and_clearer_without_a_device(lib):
+    """mb_device_status / mb_clear_device_status allocate nothing: with no
+    status word on the current device (or no device at all) they report a
+    clean 0 and succeed."""
+    import ctypes
+    v = ctypes.c_uint32(123)
+    assert lib.mb_device_status(ctypes.byref(v)) == 0
+    assert v.value == 0
+    assert lib.mb_clear_device_status() == 0

@@ -44,6 +44,11 @@ def test_noalloc_matches_workspace_entry_point_twice():
         assert rel <= 1e-4, rel
         truth = O.sqr_mm(A, B, acc=np.float64)
         assert np.abs(got - truth).max() / np.abs(truth).max() <= 1e-4
+        # a clean call leaves no bounded-wait timeout on the device
+        import ctypes
+        from metalbench_b200 import _lib
+        st = ctypes.c_uint32(1)
+        assert _lib.lib().mb_device_status(ctypes.byref(st)) == 0 and st.value == 0
 
 
 def test_noalloc_rejects_shapes_beyond_the_fixed_array():
