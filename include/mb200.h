@@ -175,6 +175,19 @@ int mb_sqr_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N
 int mb_conv2d_nhwc_bf16(const uint16_t* x, const uint16_t* w, uint16_t* y, int N, int H, int W,
                         int Cin, int Cout, int KH, int KW, int stride, int pad, void* stream);
 
+/* fp32 conv2d for the reference's own conv2d_f32 entry (registry
+ * mlx/kernels/common/registry.py:469-477: x (8,64,64,64), w (128,3,3,64),
+ * pad 0, rtol = atol = 1e-3). Same layouts as the bf16 entry, fp32 buffers,
+ * any stride >= 1 and pad >= 0, Cin % 4 == 0, 16-byte aligned x and w. The
+ * products use 3xTF32 (fp32-accurate) on the tcgen05 GEMM: an im2col pass
+ * writes the tf32-split patch matrix into `workspace`
+ * (mb_conv2d_nhwc_f32_workspace_bytes, 256-byte aligned, caller owned). */
+size_t mb_conv2d_nhwc_f32_workspace_bytes(int N, int H, int W, int Cin, int Cout, int KH, int KW,
+                                          int stride, int pad);
+int mb_conv2d_nhwc_f32(const float* x, const float* w, float* y, int N, int H, int W, int Cin,
+                       int Cout, int KH, int KW, int stride, int pad, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* ---- GQA attention over a paged KV cache (hook
  *      mlx/kernels/full/llama_decoder_layer.py:30-37) ----------------------
  * Cache: k_cache, v_cache = [num_pages][Hkv][64][Dh] bf16; token p of
@@ -231,6 +244,21 @@ int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, 
                              uint16_t* k_cache, uint16_t* v_cache, const int* block_table,
                              int max_pages, int causal, void* workspace, size_t workspace_bytes,
                              void* stream);
+
+/* fp32 decoder layer for the reference's own llama_decoder_layer_f32 entry
+ * (mlx/kernels/full/llama_decoder_layer.py:24-64; registry
+ * mlx/kernels/full/registry.py:87-104: S 64, D 128, H 4 / H_kv 2, head_dim 32,
+ * FF 256, rtol = atol = 1e-2). x, y [B*S, D] fp32; weights fp32 in the
+ * reference (in, out) layout; head_dim = D/H even and <= 256, D and FF
+ * multiples of 4. Every sequence's tokens sit at positions 0..S-1; causal = 0
+ * is the reference hook. GEMMs run in 3xTF32 (fp32-accurate); norms, RoPE,
+ * softmax and SwiGLU in fp32. Scratch: mb_llama_decoder_f32_workspace_bytes,
+ * 256-byte aligned, caller owned. */
+size_t mb_llama_decoder_f32_workspace_bytes(int B, int S, int D, int H, int H_kv, int FF);
+int mb_llama_decoder_f32(const float* x, const float* W_qkv, const float* W_o, const float* W_gu,
+                         const float* W_down, float* y, int B, int S, int D, int H, int H_kv,
+                         int FF, float rope_base, float eps, int causal, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* In-place bf16 sum all-reduce over the tensor-parallel communicator. */
 int mb_tp_allreduce_bf16(uint16_t* buf, size_t count, void* stream);

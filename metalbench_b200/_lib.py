@@ -85,6 +85,11 @@ SIGNATURES = {
     "mb_batch_mm_f32_workspace_bytes": (C.c_size_t, [_I64, _I64, _I64, _I64]),
     "mb_batch_mm_f32": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, C.c_size_t, _P]),
     "mb_conv2d_nhwc_bf16": (C.c_int, [_P, _P, _P] + [_I] * 9 + [_P]),
+    "mb_conv2d_nhwc_f32_workspace_bytes": (C.c_size_t, [_I] * 9),
+    "mb_conv2d_nhwc_f32": (C.c_int, [_P, _P, _P] + [_I] * 9 + [_P, C.c_size_t, _P]),
+    "mb_llama_decoder_f32_workspace_bytes": (C.c_size_t, [_I] * 6),
+    "mb_llama_decoder_f32": (C.c_int, [_P] * 6 + [_I] * 6 + [C.c_float, C.c_float, _I, _P,
+                                                            C.c_size_t, _P]),
     "mb_attention_decode_workspace_bytes": (C.c_size_t, [_I, _I, _I, _I]),
     "mb_attention_decode_bf16": (C.c_int, [_P, _I, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _I,
                                            _P, C.c_size_t, _P]),

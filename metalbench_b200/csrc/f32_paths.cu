@@ -1,0 +1,395 @@
+// fp32-accurate paths for the reference's own fp32 registry entries, so that a
+// manifest the reference harness builds (f32 buffers, mlx/scripts/
+// mlx_helpers.py:236-263, 290-335) runs unchanged:
+//
+//   mb_conv2d_nhwc_f32      conv2d_f32 (mlx/kernels/common/registry.py:469-477:
+//                           x (8,64,64,64) * w (128,3,3,64), pad 0, rtol/atol 1e-3)
+//   mb_llama_decoder_f32    llama_decoder_layer_f32 (mlx/kernels/full/registry.py:
+//                           87-104: S 64, D 128, H 4 / H_kv 2, head_dim 32, FF 256,
+//                           rtol/atol 1e-2), any even head_dim <= 256
+//
+// Both run their contractions on the 3xTF32 tcgen05 GEMM (hi/lo tf32 split,
+// lo*hi + hi*lo + hi*hi accumulated in fp32 in TMEM), which keeps fp32
+// accuracy; nothing is computed in plain TF32 or bf16.
+//
+// conv2d: an im2col pass writes the patch matrix [N*H2*W2, KH*KW*Cin] already
+// split into hi/lo (K-major, the GEMM's A operand); the OHWI weights are the
+// K-major B operand as they lie ([Cout, KH*KW*Cin]), so they are only split.
+//
+// decoder: mlx/kernels/full/llama_decoder_layer.py:24-64 in its own order:
+// RMSNorm (no gain) -> h @ W_qkv -> interleaved RoPE on q, k (pairs 2i, 2i+1,
+// omega_i = base^(-2i/Dh), positions 0..S-1 of each sequence) -> GQA softmax
+// attention (query head h reads kv head h / G) -> @ W_o + x -> RMSNorm ->
+// h @ W_gu -> silu(gate) * up -> @ W_down + residual.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---------------------------------------------------------------------------
+// conv2d im2col + tf32 split: row m = (n, oh, ow), column k = (r, s, c4*4..+3).
+// Each thread handles 4 channels (16 bytes) of one (m, r, s); out-of-image
+// taps are zero (the padding).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split4(const float4 x, float4& h, float4& l) {
+  h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+  h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+  h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+  h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+  l.x = x.x - h.x;
+  l.y = x.y - h.y;
+  l.z = x.z - h.z;
+  l.w = x.w - h.w;
+}
+
+__global__ void __launch_bounds__(256) im2col_split_kernel(
+    const float* __restrict__ x, float4* __restrict__ a_hi, float4* __restrict__ a_lo, int H,
+    int W, int Ci, int H2, int W2, int KH, int KW, int stride, int pad, int64_t total4) {
+  const int c4n = Ci / 4;
+  const int64_t row4 = (int64_t)KH * KW * c4n;  // float4 per patch row
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / row4;
+    const int rem = (int)(i - m * row4);
+    const int c4 = rem % c4n;
+    const int rs = rem / c4n;
+    const int s = rs % KW, r = rs / KW;
+    const int ow = (int)(m % W2);
+    const int64_t t = m / W2;
+    const int oh = (int)(t % H2);
+    const int64_t n = t / H2;
+    const int ih = oh * stride + r - pad, iw = ow * stride + s - pad;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+      v = *reinterpret_cast<const float4*>(x + (((n * H + ih) * W + iw) * Ci) + c4 * 4);
+    float4 h, l;
+    split4(v, h, l);
+    a_hi[i] = h;
+    a_lo[i] = l;
+  }
+}
+
+struct ConvGeom {
+  int64_t M, K, H2, W2;
+};
+
+int conv_geom(int N, int H, int W, int Ci, int Co, int KH, int KW, int stride, int pad,
+              ConvGeom* g) {
+  MB_REQUIRE(N >= 0 && H > 0 && W > 0 && Ci > 0 && Co > 0 && KH > 0 && KW > 0,
+             "mb_conv2d_nhwc_f32: non-positive dimension");
+  MB_REQUIRE(stride >= 1 && pad >= 0, "mb_conv2d_nhwc_f32: stride must be >= 1, pad >= 0");
+  MB_REQUIRE(Ci % 4 == 0, "mb_conv2d_nhwc_f32: Cin must be a multiple of 4");
+  g->H2 = (H + 2 * pad - KH) / stride + 1;
+  g->W2 = (W + 2 * pad - KW) / stride + 1;
+  MB_REQUIRE(H + 2 * pad >= KH && W + 2 * pad >= KW, "mb_conv2d_nhwc_f32: filter larger than input");
+  g->M = (int64_t)N * g->H2 * g->W2;
+  g->K = (int64_t)KH * KW * Ci;
+  return MB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// decoder pieces (fp32)
+// ---------------------------------------------------------------------------
+// out[r] = x[r] * rsqrt(mean(x[r]^2) + eps), one warp per row
+__global__ void rmsnorm_f32_kernel(const float* __restrict__ x, float* __restrict__ out, int M,
+                                   int D, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= M) return;
+  const float* xr = x + (int64_t)warp * D;
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) ss = fmaf(xr[c], xr[c], ss);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)D + eps);
+  float* orow = out + (int64_t)warp * D;
+  for (int c = lane; c < D; c += 32) orow[c] = xr[c] * r;
+}
+
+// qkv [B*S, D + 2*Hkv*Dh] -> q [B][H][S][Dh], k [B][Hkv][S][Dh] (both rotated),
+// v [B][Hkv][S][Dh]. One thread per (row, pair) of the q|k|v columns.
+__global__ void rope_split_f32_kernel(const float* __restrict__ qkv, float* __restrict__ q,
+                                      float* __restrict__ k, float* __restrict__ v, int B, int S,
+                                      int H, int Hkv, int Dh, double log2_base) {
+  const int D = H * Dh;
+  const int ncol = D + 2 * Hkv * Dh;
+  const int pairs = ncol / 2;
+  const int64_t total = (int64_t)B * S * pairs;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / pairs;
+    const int col = (int)(i - row * pairs) * 2;
+    const int b = (int)(row / S), s = (int)(row % S);
+    const float x0 = qkv[row * ncol + col], x1 = qkv[row * ncol + col + 1];
+    int head, d;
+    float* dst;
+    int nh;
+    bool rot = true;
+    if (col < D) {
+      head = col / Dh, d = col % Dh, dst = q, nh = H;
+    } else if (col < D + Hkv * Dh) {
+      head = (col - D) / Dh, d = (col - D) % Dh, dst = k, nh = Hkv;
+    } else {
+      head = (col - D - Hkv * Dh) / Dh, d = (col - D - Hkv * Dh) % Dh, dst = v, nh = Hkv;
+      rot = false;
+    }
+    float r0 = x0, r1 = x1;
+    if (rot) {
+      // omega_i = base^(-2i/Dh) for pair i = d/2; angle in double, then fp32
+      const double omega = exp2(-(double)d / (double)Dh * log2_base);
+      double sn, cs;
+      sincos((double)s * omega, &sn, &cs);
+      const float c = (float)cs, sf = (float)sn;
+      r0 = x0 * c - x1 * sf;
+      r1 = x0 * sf + x1 * c;
+    }
+    float* o = dst + (((int64_t)b * nh + head) * S + s) * Dh + d;
+    o[0] = r0;
+    o[1] = r1;
+  }
+}
+
+// o[b*S+i][h*Dh + d] = softmax_j(q_i . k_j / sqrt(Dh)) v_j over keys j < S
+// (j <= i when causal); one warp per query row, online softmax over chunks of
+// 32 keys (lane t scores key j0+t), each lane owning dims lane, lane+32, ...
+constexpr int kMaxDhF32 = 256;
+__global__ void __launch_bounds__(128) attention_f32_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    float* __restrict__ o, int S, int H, int Hkv, int Dh, int causal, float scale) {
+  __shared__ float qs[4][kMaxDhF32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 4 + w;
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (i >= S) return;
+  const int G = H / Hkv, kh = h / G;
+  const float* qr = q + (((int64_t)b * H + h) * S + i) * Dh;
+  for (int d = lane; d < Dh; d += 32) qs[w][d] = qr[d] * scale;
+  __syncwarp();
+  const float* kb = k + ((int64_t)b * Hkv + kh) * S * Dh;
+  const float* vb = v + ((int64_t)b * Hkv + kh) * S * Dh;
+  const int nkeys = causal ? i + 1 : S;
+  constexpr int DPL = kMaxDhF32 / 32;  // dims per lane at most
+  float acc[DPL];
+#pragma unroll
+  for (int t = 0; t < DPL; ++t) acc[t] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  for (int j0 = 0; j0 < nkeys; j0 += 32) {
+    const int j = j0 + lane;
+    float sc = -INFINITY;
+    if (j < nkeys) {
+      const float* kr = kb + (int64_t)j * Dh;
+      float dot = 0.f;
+      for (int d = 0; d < Dh; ++d) dot = fmaf(qs[w][d], kr[d], dot);
+      sc = dot;
+    }
+    float cm = sc;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+    const float mn = fmaxf(m, cm);
+    const float corr = expf(m - mn);  // 0 on the first chunk (m = -inf)
+    const float p = j < nkeys ? expf(sc - mn) : 0.f;
+    float ps = p;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+    l = l * corr + ps;
+    m = mn;
+#pragma unroll
+    for (int t = 0; t < DPL; ++t) acc[t] *= corr;
+    const int nj = nkeys - j0 < 32 ? nkeys - j0 : 32;
+    for (int tt = 0; tt < nj; ++tt) {
+      const float pt = __shfl_sync(0xffffffffu, p, tt);
+      const float* vr = vb + (int64_t)(j0 + tt) * Dh;
+#pragma unroll
+      for (int t = 0; t < DPL; ++t) {
+        const int d = lane + 32 * t;
+        if (d < Dh) acc[t] = fmaf(pt, vr[d], acc[t]);
+      }
+    }
+  }
+  const float inv = 1.f / l;
+  float* orow = o + ((int64_t)b * S + i) * (H * Dh) + h * Dh;
+#pragma unroll
+  for (int t = 0; t < DPL; ++t) {
+    const int d = lane + 32 * t;
+    if (d < Dh) orow[d] = acc[t] * inv;
+  }
+}
+
+__global__ void add_f32_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                               float* __restrict__ out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = a[i] + b[i];
+}
+
+// act[r][c] = silu(gu[r][c]) * gu[r][FF + c]
+__global__ void swiglu_f32_kernel(const float* __restrict__ gu, float* __restrict__ act,
+                                  int64_t rows, int FF) {
+  const int64_t n = rows * FF;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / FF;
+    const int c = (int)(i - r * FF);
+    const float g = gu[r * 2 * FF + c], u = gu[r * 2 * FF + FF + c];
+    act[i] = g / (1.f + expf(-g)) * u;
+  }
+}
+
+int grid_for(int64_t n) {
+  const int64_t want = (n + 255) / 256;
+  const int64_t cap = (int64_t)mb::num_sms() * 16;
+  return (int)(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+struct DecF32Layout {
+  size_t h, qkv, q, k, v, attn, x1, tmp, gu, act, gemm, total;
+};
+
+DecF32Layout dec_f32_layout(int64_t B, int64_t S, int64_t D, int64_t H, int64_t Hkv,
+                            int64_t FF) {
+  const int64_t Dh = D / H, R = B * S, nqkv = D + 2 * Hkv * Dh;
+  DecF32Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += al256(bytes);
+    return o;
+  };
+  L.h = take(R * D * 4);
+  L.qkv = take(R * nqkv * 4);
+  L.q = take(R * D * 4);
+  L.k = take(R * Hkv * Dh * 4);
+  L.v = take(R * Hkv * Dh * 4);
+  L.attn = take(R * D * 4);
+  L.x1 = take(R * D * 4);
+  L.tmp = take(R * D * 4);
+  L.gu = take(R * 2 * FF * 4);
+  L.act = take(R * FF * 4);
+  size_t g = mb_sqr_mm_f32_workspace_bytes(R, nqkv, D);
+  const size_t g2 = mb_sqr_mm_f32_workspace_bytes(R, D, D);
+  const size_t g3 = mb_sqr_mm_f32_workspace_bytes(R, 2 * FF, D);
+  const size_t g4 = mb_sqr_mm_f32_workspace_bytes(R, D, FF);
+  g = g > g2 ? g : g2;
+  g = g > g3 ? g : g3;
+  g = g > g4 ? g : g4;
+  L.gemm = take(g);
+  L.total = off;
+  return L;
+}
+
+int dec_f32_check(int64_t B, int64_t S, int64_t D, int64_t H, int64_t Hkv, int64_t FF) {
+  MB_REQUIRE(B >= 1 && S >= 1 && D >= 1 && H >= 1 && Hkv >= 1 && FF >= 1,
+             "mb_llama_decoder_f32: non-positive dimension");
+  MB_REQUIRE(D % H == 0 && H % Hkv == 0, "mb_llama_decoder_f32: D %% H and H %% H_kv must be 0");
+  const int64_t Dh = D / H;
+  MB_REQUIRE(Dh % 2 == 0 && Dh <= kMaxDhF32, "mb_llama_decoder_f32: head_dim must be even and <= %d",
+             kMaxDhF32);
+  MB_REQUIRE(D % 4 == 0 && FF % 4 == 0 && (Hkv * Dh) % 2 == 0,
+             "mb_llama_decoder_f32: D and FF must be multiples of 4");
+  return MB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t mb_conv2d_nhwc_f32_workspace_bytes(int N, int H, int W, int Cin, int Cout,
+                                                     int KH, int KW, int stride, int pad) {
+  ConvGeom g;
+  if (conv_geom(N, H, W, Cin, Cout, KH, KW, stride, pad, &g)) return 0;
+  return 2 * al256((size_t)g.M * g.K * 4) + 2 * al256((size_t)Cout * g.K * 4);
+}
+
+extern "C" int mb_conv2d_nhwc_f32(const float* x, const float* w, float* y, int N, int H, int W,
+                                  int Cin, int Cout, int KH, int KW, int stride, int pad,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  ConvGeom g;
+  int rc = conv_geom(N, H, W, Cin, Cout, KH, KW, stride, pad, &g);
+  if (rc) return rc;
+  if (g.M == 0) return MB_OK;
+  const size_t need = mb_conv2d_nhwc_f32_workspace_bytes(N, H, W, Cin, Cout, KH, KW, stride, pad);
+  MB_REQUIRE(workspace && workspace_bytes >= need &&
+                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "mb_conv2d_nhwc_f32: workspace of %zu bytes (256-byte aligned) required, got %zu",
+             need, workspace_bytes);
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0,
+             "mb_conv2d_nhwc_f32: x and w must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* a_hi = reinterpret_cast<float*>(ws);
+  float* a_lo = reinterpret_cast<float*>(ws + al256((size_t)g.M * g.K * 4));
+  float* b_hi = reinterpret_cast<float*>(ws + 2 * al256((size_t)g.M * g.K * 4));
+  float* b_lo = reinterpret_cast<float*>(ws + 2 * al256((size_t)g.M * g.K * 4) +
+                                         al256((size_t)Cout * g.K * 4));
+  const int64_t total4 = g.M * g.K / 4;
+  im2col_split_kernel<<<grid_for(total4), 256, 0, s>>>(
+      x, reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), H, W, Cin, (int)g.H2,
+      (int)g.W2, KH, KW, stride, pad, total4);
+  MB_CUDA(cudaGetLastError());
+  rc = mb::tf32x3_split_rows(w, b_hi, b_lo, (int64_t)Cout * g.K, s);
+  if (rc) return rc;
+  return mb::tf32x3_core(a_hi, a_lo, b_hi, b_lo, y, 1, g.M, Cout, g.K, mb::device_status_ptr(),
+                         s);
+}
+
+extern "C" size_t mb_llama_decoder_f32_workspace_bytes(int B, int S, int D, int H, int H_kv,
+                                                       int FF) {
+  if (dec_f32_check(B, S, D, H, H_kv, FF)) return 0;
+  return dec_f32_layout(B, S, D, H, H_kv, FF).total;
+}
+
+extern "C" int mb_llama_decoder_f32(const float* x, const float* W_qkv, const float* W_o,
+                                    const float* W_gu, const float* W_down, float* y, int B, int S,
+                                    int D, int H, int H_kv, int FF, float rope_base, float eps,
+                                    int causal, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  int rc = dec_f32_check(B, S, D, H, H_kv, FF);
+  if (rc) return rc;
+  const DecF32Layout L = dec_f32_layout(B, S, D, H, H_kv, FF);
+  MB_REQUIRE(workspace && workspace_bytes >= L.total &&
+                 reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "mb_llama_decoder_f32: workspace of %zu bytes (256-byte aligned) required, got %zu",
+             L.total, workspace_bytes);
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0, "mb_llama_decoder_f32: x must be 16-byte aligned");
+  MB_REQUIRE(rope_base > 0.f, "mb_llama_decoder_f32: rope base must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto F = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
+  float *h = F(L.h), *qkv = F(L.qkv), *q = F(L.q), *k = F(L.k), *v = F(L.v), *attn = F(L.attn),
+        *x1 = F(L.x1), *tmp = F(L.tmp), *gu = F(L.gu), *act = F(L.act);
+  void* gws = ws + L.gemm;
+  const size_t gwsb = L.total - L.gemm;
+  const int64_t R = (int64_t)B * S;
+  const int Dh = D / H;
+  const int nqkv = D + 2 * H_kv * Dh;
+  const int rows_grid = (int)((R * 32 + 255) / 256);
+
+  rmsnorm_f32_kernel<<<rows_grid, 256, 0, s>>>(x, h, (int)R, D, eps);
+  MB_CUDA(cudaGetLastError());
+  rc = mb_sqr_mm_f32(h, W_qkv, qkv, R, nqkv, D, gws, gwsb, s);
+  if (rc) return rc;
+  const int64_t pairs = R * (nqkv / 2);
+  rope_split_f32_kernel<<<grid_for(pairs), 256, 0, s>>>(qkv, q, k, v, B, S, H, H_kv, Dh,
+                                                         log2((double)rope_base));
+  MB_CUDA(cudaGetLastError());
+  const float scale = (float)(1.0 / sqrt((double)Dh));
+  attention_f32_kernel<<<dim3((unsigned)((S + 3) / 4), (unsigned)H, (unsigned)B), 128, 0, s>>>(
+      q, k, v, attn, S, H, H_kv, Dh, causal, scale);
+  MB_CUDA(cudaGetLastError());
+  rc = mb_sqr_mm_f32(attn, W_o, tmp, R, D, D, gws, gwsb, s);
+  if (rc) return rc;
+  add_f32_kernel<<<grid_for(R * D), 256, 0, s>>>(x, tmp, x1, R * D);
+  MB_CUDA(cudaGetLastError());
+  rmsnorm_f32_kernel<<<rows_grid, 256, 0, s>>>(x1, h, (int)R, D, eps);
+  MB_CUDA(cudaGetLastError());
+  rc = mb_sqr_mm_f32(h, W_gu, gu, R, 2 * FF, D, gws, gwsb, s);
+  if (rc) return rc;
+  swiglu_f32_kernel<<<grid_for(R * FF), 256, 0, s>>>(gu, act, R, FF);
+  MB_CUDA(cudaGetLastError());
+  rc = mb_sqr_mm_f32(act, W_down, tmp, R, D, FF, gws, gwsb, s);
+  if (rc) return rc;
+  add_f32_kernel<<<grid_for(R * D), 256, 0, s>>>(x1, tmp, y, R * D);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}

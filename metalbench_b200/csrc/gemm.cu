@@ -136,28 +136,30 @@ size_t tf32x3_workspace(int64_t batch, int64_t M, int64_t N, int64_t K) {
   return 2 * align256((size_t)batch * M * K * 4) + 2 * align256((size_t)batch * N * K * 4);
 }
 
-// C[b] = A[b] @ B[b] for b < batch (row-major, contiguous batches) with
-// 3xTF32: split prepass into the workspace, then one persistent GEMM launch
-// whose tile rows run over all batches. M % 128 == 0 when batch > 1, so no
-// 128-row tile straddles two batches; B rows of batch b start at b*N in the
-// transposed operand (GemmProducer::b_rows_per_batch).
-int tf32x3_gemm(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t N,
-                int64_t K, uint8_t* w, uint32_t* status, cudaStream_t s) {
-  float* a_hi = reinterpret_cast<float*>(w);
-  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)batch * M * K * 4));
-  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)batch * M * K * 4));
-  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)batch * M * K * 4) +
-                                         align256((size_t)batch * N * K * 4));
-  const int sms = mb::num_sms();
-  split_a_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(A),
-                                          reinterpret_cast<float4*>(a_hi),
-                                          reinterpret_cast<float4*>(a_lo), batch * M * K / 4);
-  MB_CUDA(cudaGetLastError());
-  dim3 g((unsigned)((N + 63) / 64), (unsigned)((K + 63) / 64), (unsigned)batch);
-  MB_REQUIRE(g.y <= 65535 && g.z <= 65535, "tf32x3: K or batch too large");
-  split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
-  MB_CUDA(cudaGetLastError());
+}  // namespace
 
+namespace mb {
+
+int tf32x3_split_rows(const float* src, float* hi, float* lo, int64_t n, cudaStream_t s) {
+  MB_REQUIRE(n % 4 == 0, "tf32x3 split: element count must be a multiple of 4");
+  MB_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0, "tf32x3 split: source must be 16-byte aligned");
+  if (n == 0) return MB_OK;
+  const int sms = mb::num_sms();
+  split_a_kernel<<<sms * 8, 256, 0, s>>>(reinterpret_cast<const float4*>(src),
+                                         reinterpret_cast<float4*>(hi),
+                                         reinterpret_cast<float4*>(lo), n / 4);
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+// C[b] = A[b] @ B[b] for b < batch from operands split already: A_hi/A_lo
+// [batch*M, K] and B_hi/B_lo [batch*N, K], both K-major. M % 128 == 0 when
+// batch > 1, so no 128-row tile straddles two batches; B rows of batch b
+// start at b*N (GemmProducer::b_rows_per_batch).
+int tf32x3_core(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                float* C, int64_t batch, int64_t M, int64_t N, int64_t K, uint32_t* status,
+                cudaStream_t s) {
+  const int sms = mb::num_sms();
   using P = GemmProducer<Mode::TF32X3, 128, false>;
   using S = Smem<P, 128, 3>;
   gemm::Epi<128, gemm::EpiStore> e{};
@@ -195,6 +197,29 @@ int tf32x3_gemm(const float* A, const float* B, float* C, int64_t batch, int64_t
   kern<<<grid, 256, S::TOTAL, s>>>(p, e, sc, status);
   MB_CUDA(cudaGetLastError());
   return MB_OK;
+}
+
+}  // namespace mb
+
+namespace {
+
+// C[b] = A[b] @ B[b] for b < batch (row-major, contiguous batches) with
+// 3xTF32: split prepass into the workspace (B transposed to K-major), then
+// one persistent GEMM launch whose tile rows run over all batches.
+int tf32x3_gemm(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t N,
+                int64_t K, uint8_t* w, uint32_t* status, cudaStream_t s) {
+  float* a_hi = reinterpret_cast<float*>(w);
+  float* a_lo = reinterpret_cast<float*>(w + align256((size_t)batch * M * K * 4));
+  float* b_hi = reinterpret_cast<float*>(w + 2 * align256((size_t)batch * M * K * 4));
+  float* b_lo = reinterpret_cast<float*>(w + 2 * align256((size_t)batch * M * K * 4) +
+                                         align256((size_t)batch * N * K * 4));
+  int rc = mb::tf32x3_split_rows(A, a_hi, a_lo, batch * M * K, s);
+  if (rc) return rc;
+  dim3 g((unsigned)((N + 63) / 64), (unsigned)((K + 63) / 64), (unsigned)batch);
+  MB_REQUIRE(g.y <= 65535 && g.z <= 65535, "tf32x3: K or batch too large");
+  split_bt_kernel<<<g, 256, 0, s>>>(B, b_hi, b_lo, K, N);
+  MB_CUDA(cudaGetLastError());
+  return mb::tf32x3_core(a_hi, a_lo, b_hi, b_lo, C, batch, M, N, K, status, s);
 }
 
 int check_tf32x3_args(const char* fn, const float* A, int64_t batch, int64_t M, int64_t N,

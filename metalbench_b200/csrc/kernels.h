@@ -67,6 +67,14 @@ int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 int gemm_bf16_ex(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N,
                  int64_t K, int64_t ldc, int b_layout, const uint16_t* residual, int64_t ld_res,
                  int act, cudaStream_t s);
+// gemm.cu: 3xTF32 pieces. tf32x3_split_rows splits n fp32 values (n % 4 == 0,
+// 16-byte aligned) into tf32 hi and the exact fp32 remainder lo;
+// tf32x3_core runs C[batch*M, N] (fp32, row stride N) = A @ B^T from K-major
+// split operands A_hi/A_lo [batch*M, K], B_hi/B_lo [batch*N, K].
+int tf32x3_split_rows(const float* src, float* hi, float* lo, int64_t n, cudaStream_t s);
+int tf32x3_core(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                float* C, int64_t batch, int64_t M, int64_t N, int64_t K, uint32_t* status,
+                cudaStream_t s);
 // attention_tc.cu: tcgen05 prefill attention (same contract as
 // mb_attention_prefill_bf16, Dh = 128); _ok() says whether TMA can address
 // the operands.

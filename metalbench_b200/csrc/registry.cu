@@ -193,8 +193,34 @@ int prep_conv2d(const RunArgs& a, KernelState& st, cudaStream_t) {
   double padv = a.config.num("padding", 0);
   a.scalar(11, &padv);
   const int64_t pad = (int64_t)padv;
+  if (x->dtype == MB_F32) {
+    // the reference's own conv2d_f32 entry: fp32 buffers, 3xTF32 products
+    MB_REQUIRE(w->dtype == MB_F32 && y->dtype == MB_F32, "conv2d: mixed f32/bf16 buffers");
+    MB_REQUIRE(stride >= 1, "conv2d: stride must be >= 1");
+    const int64_t H2 = (H + 2 * pad - KH) / stride + 1, W2 = (W + 2 * pad - KW) / stride + 1;
+    MB_REQUIRE(x->bytes == (size_t)(N * H * W * Ci * 4) &&
+                   w->bytes == (size_t)(Co * KH * KW * Ci * 4) &&
+                   y->bytes == (size_t)(N * H2 * W2 * Co * 4),
+               "conv2d: buffer sizes do not match the geometry");
+    const size_t wsb = mb_conv2d_nhwc_f32_workspace_bytes((int)N, (int)H, (int)W, (int)Ci, (int)Co,
+                                                          (int)KH, (int)KW, (int)stride, (int)pad);
+    MB_REQUIRE(wsb > 0, "conv2d: unsupported f32 geometry (Cin must be a multiple of 4)");
+    void* ws = nullptr;
+    MB_CUDA(cudaMalloc(&ws, wsb));
+    st.scratch.push_back(ws);
+    const void *px = x->dev, *pw = w->dev;
+    void* py = y->dev;
+    st.threads_per_cta = 256;
+    st.launches_per_iter = 3;
+    st.launch = [=](cudaStream_t s) {
+      return mb_conv2d_nhwc_f32((const float*)px, (const float*)pw, (float*)py, (int)N, (int)H,
+                                (int)W, (int)Ci, (int)Co, (int)KH, (int)KW, (int)stride, (int)pad,
+                                ws, wsb, s);
+    };
+    return MB_OK;
+  }
   MB_REQUIRE(x->dtype == MB_BF16 && w->dtype == MB_BF16 && y->dtype == MB_BF16,
-             "conv2d: buffers must be bf16");
+             "conv2d: buffers must be all bf16 or all f32");
   const int64_t H2 = H + 2 * pad - KH + 1, W2 = W + 2 * pad - KW + 1;
   MB_REQUIRE(x->bytes == (size_t)(N * H * W * Ci * 2) && w->bytes == (size_t)(Co * KH * KW * Ci * 2) &&
                  y->bytes == (size_t)(N * H2 * W2 * Co * 2),
@@ -239,8 +265,42 @@ int prep_llama(const RunArgs& a, KernelState& st, cudaStream_t stream) {
   const int causal = (int)a.config.num("causal", 0);
   const int past = (int)a.config.num("past_len", 0);
   MB_REQUIRE(B >= 1 && S >= 1 && past >= 0, "llama_decoder_layer: bad batch/S/past_len");
+  if (x->dtype == MB_F32) {
+    // the reference's own llama_decoder_layer_f32 entry: fp32 buffers, any
+    // even head_dim <= 256 (the registry's is 32), no KV cache
+    for (const RunArgs::Buf* b : {wq, wo, wg, wd, y})
+      MB_REQUIRE(b->dtype == MB_F32, "llama_decoder_layer: mixed f32/bf16 buffers");
+    MB_REQUIRE(past == 0, "llama_decoder_layer: past_len needs the bf16 path");
+    MB_REQUIRE(H > 0 && D % H == 0, "llama_decoder_layer: D must be a multiple of H");
+    const int64_t Dh = D / H;
+    MB_REQUIRE(x->bytes == (size_t)(B * S * D * 4) && y->bytes == x->bytes,
+               "llama_decoder_layer: x/y must be [batch*S, D] f32");
+    MB_REQUIRE(wq->bytes == (size_t)(D * (D + 2 * Hkv * Dh) * 4) &&
+                   wo->bytes == (size_t)(D * D * 4) && wg->bytes == (size_t)(D * 2 * FF * 4) &&
+                   wd->bytes == (size_t)(FF * D * 4),
+               "llama_decoder_layer: weight sizes do not match D/H/H_kv/FF");
+    const size_t wsb = mb_llama_decoder_f32_workspace_bytes(B, (int)S, (int)D, (int)H, (int)Hkv,
+                                                            (int)FF);
+    MB_REQUIRE(wsb > 0, "llama_decoder_layer: unsupported f32 geometry (head_dim even <= 256, "
+                        "D and FF multiples of 4)");
+    void* ws = nullptr;
+    MB_CUDA(cudaMalloc(&ws, wsb));
+    st.scratch.push_back(ws);
+    const float *px = (const float*)x->dev, *pq = (const float*)wq->dev,
+                *po = (const float*)wo->dev, *pg = (const float*)wg->dev,
+                *pd = (const float*)wd->dev;
+    float* py = (float*)y->dev;
+    const float fb = (float)base, fe = (float)eps;
+    st.threads_per_cta = 256;
+    st.launches_per_iter = 0;
+    st.launch = [=](cudaStream_t s) {
+      return mb_llama_decoder_f32(px, pq, po, pg, pd, py, B, (int)S, (int)D, (int)H, (int)Hkv,
+                                  (int)FF, fb, fe, causal, ws, wsb, s);
+    };
+    return MB_OK;
+  }
   for (const RunArgs::Buf* b : {x, wq, wo, wg, wd, y})
-    MB_REQUIRE(b->dtype == MB_BF16, "llama_decoder_layer: buffers must be bf16");
+    MB_REQUIRE(b->dtype == MB_BF16, "llama_decoder_layer: buffers must be all bf16 or all f32");
   const int Dh = (int)(D / H);
   MB_REQUIRE(x->bytes == (size_t)(B * S * D * 2) && y->bytes == x->bytes,
              "llama_decoder_layer: x/y must be [batch*S, D] bf16");

@@ -44,6 +44,10 @@ KERNEL_SOURCES = {
     "mha_attention": ["fused_ops.cu", "attention.cu", "gemm.cu"],
     "transformer_block": ["fused_ops.cu", "attention.cu", "gemm.cu", "gemm_epi.cuh"],
 }
+# registry entries whose buffers take another path of the same mb_run kernel
+# (the fp32 entries of the reference: conv2d_f32, llama_decoder_layer_f32)
+DTYPE_SOURCES = {"f32": {"conv2d": ["f32_paths.cu", "gemm.cu", "gemm_core.cuh"],
+                         "llama_decoder_layer": ["f32_paths.cu", "gemm.cu", "gemm_core.cuh"]}}
 # files every kernel depends on
 SHARED_SOURCES = ["common.cuh", "abi.cu", "registry.cu", "kernels.h"]
 
@@ -158,7 +162,9 @@ def kernels_for(paths: list[str]) -> list[str]:
             if fname in SHARED_SOURCES:
                 names.update(reg)
             for n, v in reg.items():
-                if fname in KERNEL_SOURCES.get(v["kernel"], []):
+                dt = (v.get("input_dtypes") or ["f32"])[0]
+                srcs = DTYPE_SOURCES.get(dt, {}).get(v["kernel"]) or KERNEL_SOURCES.get(v["kernel"], [])
+                if fname in srcs:
                     names.add(n)
     return sorted(names)
 

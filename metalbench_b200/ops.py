@@ -146,9 +146,10 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
 
 def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, stride: int = 1, padding: int = 0,
                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """bf16 NHWC x OHWI conv2d (cross-correlation) as a tcgen05 implicit GEMM."""
-    _cuda(x, "conv2d(x)", (torch.bfloat16,))
-    _cuda(w, "conv2d(w)", (torch.bfloat16,))
+    """NHWC x OHWI conv2d (cross-correlation). bf16: tcgen05 implicit GEMM;
+    fp32: im2col + 3xTF32 GEMM (fp32-accurate, any stride / padding)."""
+    _cuda(x, "conv2d(x)", (torch.bfloat16, torch.float32))
+    _cuda(w, "conv2d(w)", (x.dtype,))
     init(x.device.index)
     N, H, W, C = x.shape
     Co, KH, KW, Ci = w.shape
@@ -157,11 +158,50 @@ def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, stride: int = 1, padding: int 
     H2 = (H + 2 * padding - KH) // stride + 1
     W2 = (W + 2 * padding - KW) // stride + 1
     if out is None:
-        out = torch.empty((N, H2, W2, Co), dtype=torch.bfloat16, device=x.device)
-    _cuda(out, "conv2d(out)", (torch.bfloat16,))
+        out = torch.empty((N, H2, W2, Co), dtype=x.dtype, device=x.device)
+    _cuda(out, "conv2d(out)", (x.dtype,))
+    if tuple(out.shape) != (N, H2, W2, Co):
+        raise ValueError("conv2d: out has the wrong shape")
+    if x.dtype == torch.float32:
+        nb = _lib.lib().mb_conv2d_nhwc_f32_workspace_bytes(N, H, W, C, Co, KH, KW, stride, padding)
+        if nb == 0:
+            raise ValueError("conv2d: unsupported fp32 geometry (Cin must be a multiple of 4)")
+        ws = _workspace(nb, x.device)
+        _lib.call("mb_conv2d_nhwc_f32", x.data_ptr(), w.data_ptr(), out.data_ptr(), N, H, W, C,
+                  Co, KH, KW, stride, padding, ws.data_ptr(), nb, _stream())
+        return out
     _lib.call("mb_conv2d_nhwc_bf16", x.data_ptr(), w.data_ptr(), out.data_ptr(), N, H, W, C, Co,
               KH, KW, stride, padding, _stream())
     return out
+
+
+def llama_decoder_f32(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor,
+                      w_gu: torch.Tensor, w_down: torch.Tensor, n_heads: int, n_kv_heads: int,
+                      base: float = 10000.0, eps: float = 1e-5, causal: bool = False) -> torch.Tensor:
+    """The reference decoder hook in fp32 (any even head_dim <= 256): x [S, D]
+    or [B, S, D], weights (in, out) fp32; tokens at positions 0..S-1."""
+    for nm, t in (("x", x), ("W_qkv", w_qkv), ("W_o", w_o), ("W_gu", w_gu), ("W_down", w_down)):
+        _cuda(t, f"llama_decoder_f32({nm})", (torch.float32,))
+    init(x.device.index)
+    X = x.unsqueeze(0) if x.dim() == 2 else x
+    B, S, D = X.shape
+    FF = w_down.shape[0]
+    Dh = D // n_heads
+    want = {"W_qkv": (D, D + 2 * n_kv_heads * Dh), "W_o": (D, D), "W_gu": (D, 2 * FF),
+            "W_down": (FF, D)}
+    for nm, t in (("W_qkv", w_qkv), ("W_o", w_o), ("W_gu", w_gu), ("W_down", w_down)):
+        if tuple(t.shape) != want[nm]:
+            raise ValueError(f"llama_decoder_f32: {nm} has shape {tuple(t.shape)}, expected {want[nm]}")
+    nb = _lib.lib().mb_llama_decoder_f32_workspace_bytes(B, S, D, n_heads, n_kv_heads, FF)
+    if nb == 0:
+        raise ValueError("llama_decoder_f32: unsupported geometry (head_dim even <= 256, "
+                         "D and FF multiples of 4)")
+    ws = _workspace(nb, x.device)
+    y = torch.empty_like(X)
+    _lib.call("mb_llama_decoder_f32", X.data_ptr(), w_qkv.data_ptr(), w_o.data_ptr(),
+              w_gu.data_ptr(), w_down.data_ptr(), y.data_ptr(), B, S, D, n_heads, n_kv_heads, FF,
+              float(base), float(eps), 1 if causal else 0, ws.data_ptr(), nb, _stream())
+    return y[0] if x.dim() == 2 else y
 
 
 def rms_norm_linear(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

@@ -61,6 +61,21 @@ REGISTRY["conv2d"] = dict(
     flops=2 * 32 * 56 * 56 * 64 * 64 * 9, bytes=2 * (32 * 56 * 56 * 64 * 2 + 64 * 9 * 64),
     roof="ridge", ref_warmup=1, ref_iters=3)
 
+# The reference's own conv2d entry (common/registry.py:469-477), served
+# unchanged next to the BASELINE one: fp32, x (8,64,64,64) * w (128,3,3,64),
+# pad 0, N(0,1) inputs (mlx_helpers.py:236-251), rtol = atol = 1e-3.
+REGISTRY["conv2d_f32"] = dict(
+    kernel="conv2d", metal_function="conv2d_f32", hook="conv2d",
+    input_bindings=(0, 1), input_shapes=[(8, 64, 64, 64), (128, 3, 3, 64)],
+    input_dtypes=["f32", "f32"], input_init=[("normal", 1.0), ("normal", 1.0)],
+    output_shape=(8, 62, 62, 128), output_dtype="f32",
+    scalars=[dict(binding=b, dtype="u32", value=v) for b, v in
+             zip(range(3, 11), (8, 64, 64, 64, 128, 3, 3, 1))],
+    model_kwargs=dict(in_channels=64, out_channels=128, kernel_size=3, stride=1),
+    rtol=1e-3, atol=1e-3, seed=0,
+    flops=8 * 128 * 62 * 62 * 64 * 9 * 2, bytes=4 * (8 * 64 * 64 * 64 + 128 * 3 * 3 * 64 + 8 * 128 * 62 * 62),
+    roof="tensor_tf32x3", ref_warmup=1, ref_iters=3)
+
 REGISTRY["gemm_bf16"] = dict(
     kernel="gemm_bf16", metal_function="rect_matmul_f32",
     input_bindings=(0, 1), input_shapes=[(4096, 4096), (4096, 4096)],

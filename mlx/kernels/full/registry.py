@@ -1,8 +1,9 @@
 """Full-set registry entries served by the B200 backend (format: see
-mlx/kernels/common/registry.py). The reference's own entry
-(mlx/kernels/full/registry.py:87-104: S=64, D=128, H=4, H_kv=2, head_dim 32)
-is replaced by the BASELINE.json decoder configurations: libmb200's decoder
-kernels need head_dim 128 and d_model a multiple of 256.
+mlx/kernels/common/registry.py). The BASELINE.json decoder configurations
+(bf16, head_dim 128) run on the fused decoder kernels; the reference's own
+entry (mlx/kernels/full/registry.py:87-104: S=64, D=128, H=4, H_kv=2,
+head_dim 32, fp32) is served next to them as ``llama_decoder_layer_f32`` on
+the fp32 path (3xTF32 GEMMs, fp32 attention).
 """
 D, H, HKV, FF, DH = 4096, 32, 8, 14336, 128
 NQKV = D + 2 * HKV * DH
@@ -52,6 +53,26 @@ REGISTRY["llama_decoder_layer_decode"] = dict(
     flops=2 * _PARAMS * _BD + 2 * 2 * _BD * H * DH * (_L + 1),
     bytes=2 * _PARAMS + 2 * 2 * _BD * HKV * _L * DH,
     roof="hbm", ref_warmup=0, ref_iters=2)
+
+# the reference's own entry, unchanged (fp32, N(0,1) inputs as
+# mlx_helpers.py:236-251 makes them, non-causal, rtol = atol = 1e-2)
+REGISTRY["llama_decoder_layer_f32"] = dict(
+    kernel="llama_decoder_layer", metal_function="llama_decoder_layer_f32",
+    hook="llama_decoder_layer",
+    input_bindings=(0, 1, 2, 3, 4),
+    input_shapes=[(64, 128), (128, 128 + 2 * 2 * 32), (128, 128), (128, 2 * 256), (256, 128)],
+    input_dtypes=["f32"] * 5, input_init=[("normal", 1.0)] * 5,
+    output_shape=(64, 128), output_dtype="f32",
+    scalars=[dict(binding=6, dtype="u32", value=64), dict(binding=7, dtype="u32", value=128),
+             dict(binding=8, dtype="u32", value=4), dict(binding=9, dtype="u32", value=2),
+             dict(binding=10, dtype="u32", value=256),
+             dict(binding=11, dtype="f32", value=10000.0),
+             dict(binding=12, dtype="f32", value=1e-5)],
+    model_kwargs=dict(S=64, D=128, H=4, H_kv=2, FF=256, base=10000.0, eps=1e-5),
+    rtol=1e-2, atol=1e-2, seed=0,
+    flops=64 * (128 * 256 * 2 + 64 * 128 * 2 + 128 * 128 * 2 + 128 * 512 * 2 + 256 * 128 * 2),
+    bytes=4 * (64 * 128 * 3 + 128 * 256 + 128 * 128 + 128 * 512 + 256 * 128),
+    roof="tensor_tf32x3", ref_warmup=2, ref_iters=10)
 
 # transformer_block (reference full/registry.py:47-62: S 64, D 128, 4 heads of
 # 32, FF 256, fp32) at a BERT-large-like B200 shape: S 4096, d_model 4096, 32

@@ -123,10 +123,13 @@ def test_decode_baseline_shape_random_cache():
     _check(_np(torch, y), ref)
 
 
-def test_prefill_baseline_shape_prefix_rows():
-    """BASELINE prefill config (batch 4 x seq 2048, causal) on the GPU; causal
-    rows 0..255 depend only on tokens 0..255, so they are checked against the
-    oracle run on that prefix."""
+def test_prefill_baseline_shape_prefix_rows_and_full_sequence():
+    """BASELINE prefill config (batch 4 x seq 2048, causal) on the GPU.
+    * rows 0..255 of every sequence depend only on tokens 0..255, so they are
+      checked against the oracle run on that prefix;
+    * sequence 0 is checked at all 2048 positions against the oracle run on
+      the whole sequence: the deep rows run all 16 key tiles of the tcgen05
+      attention, through its lazy-rescale path."""
     import torch
     from metalbench_b200.decoder import PagedKVCache
     rng = np.random.default_rng(3)
@@ -137,10 +140,14 @@ def test_prefill_baseline_shape_prefix_rows():
     cache = PagedKVCache(B, S, Hkv)
     y = layer(_bf(torch, x), cache, torch.zeros(B, dtype=torch.int32, device="cuda"))
     got = _np(torch, y)
+    assert np.isfinite(got).all()
     P = 256
     ref = O.decoder_layer(x[:, :P], *W, H=H, H_kv=Hkv, base=base, causal=True)
     _check(got[:, :P], ref)
-    assert np.isfinite(got).all()
+    ref0 = O.decoder_layer(x[:1], *W, H=H, H_kv=Hkv, base=base, causal=True)
+    _check(got[:1], ref0)
+    for lo in range(0, S, 512):  # every quarter of the sequence on its own
+        _check(got[:1, lo:lo + 512], ref0[:, lo:lo + 512])
 
 
 def test_stack_prefill_and_graph_decode_match_oracle():

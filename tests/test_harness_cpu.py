@@ -95,10 +95,13 @@ def test_compare_gate():
     b = a.copy()
     b[:5] += 1.0  # 0.5 % off
     r = Hm.compare(a, b, rtol=0.0, atol=0.1)
-    assert r["frac_within_tol"] == pytest.approx(0.995) and r["correct"] and not r["all_within"]
-    assert not Hm.compare(a, b, rtol=0, atol=0)["correct"]  # bit-exact entries need 100 %
+    # the reference verdict needs every element; the 99 % gate is reported beside it
+    assert r["frac_within_tol"] == pytest.approx(0.995) and not r["correct"] and r["gate_99"]
+    assert not r["all_within"] and r["atol_needed"] == pytest.approx(1.0)
+    assert not Hm.compare(a, b, rtol=0, atol=0)["gate_99"]  # bit-exact entries need 100 %
+    assert Hm.compare(a, b, rtol=0.0, atol=1.0)["correct"]
     b[:20] += 1.0
-    assert not Hm.compare(a, b, rtol=0.0, atol=0.1)["correct"]
+    assert not Hm.compare(a, b, rtol=0.0, atol=0.1)["gate_99"]
 
 
 def test_update_session_keeps_best_and_skips_incorrect(tmp_path, monkeypatch):

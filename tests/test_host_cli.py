@@ -58,3 +58,71 @@ def test_host_runs_reference_manifest(host, tmp_path):
     assert line["iters"] == 5 and line["chip"]["bucket"] == "b200"
     out = np.fromfile(tmp_path / "out_1.bin", dtype=np.float32).reshape(2048, 1024)
     assert out.tobytes() == np.ascontiguousarray(a.T).tobytes()
+
+
+def _manifest_for(tmp_path, function, inputs, out_shape, scalars):
+    """The manifest exactly as the reference's mlx_helpers.build_manifest
+    (mlx/scripts/mlx_helpers.py:290-335) builds it: f32 input files, the
+    output at binding len(inputs) with its byte size, u32/f32 scalars."""
+    bufs = []
+    for i, x in enumerate(inputs):
+        p = tmp_path / f"in_{i}.bin"
+        np.ascontiguousarray(x, dtype=np.float32).tofile(p)
+        bufs.append({"binding": i, "role": "input", "path": str(p)})
+    outp = tmp_path / f"out_{len(inputs)}.bin"
+    bufs.append({"binding": len(inputs), "role": "output", "path": str(outp),
+                 "size": int(np.prod(out_shape)) * 4})
+    for b, dt, v in scalars:
+        bufs.append({"binding": b, "role": "scalar", "dtype": dt, "value": v})
+    m = {"function": function, "metallib": "unused", "buffers": bufs, "grid": [65536, 1, 1],
+         "threadgroup": [1024, 1, 1], "warmup": 1, "iters": 3, "profile": False}
+    (tmp_path / "m.json").write_text(json.dumps(m))
+    return tmp_path / "m.json", outp
+
+
+def _run_manifest(host, mpath, outp, out_shape):
+    p = subprocess.run([str(host), "--manifest", str(mpath)], capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stderr
+    json.loads(p.stdout.strip().splitlines()[-1])
+    return np.fromfile(outp, dtype=np.float32).reshape(out_shape)
+
+
+@pytest.mark.gpu
+def test_host_runs_reference_conv2d_f32_manifest(host, tmp_path):
+    """The reference's conv2d entry (common/registry.py:469-477): fp32, pad 0,
+    scalars N,H,W,Cin,Cout,KH,KW,stride at bindings 3..10, rtol = atol = 1e-3
+    on every element. Checked on the committed golden (made by the reference
+    hook) and at the registry's own shape (8,64,64,64) * (128,3,3,64)."""
+    import oracle.ops as O
+    g = np.load(REPO / "tests" / "golden" / "conv2d.npz")
+    x, w, want = g["in0"], g["in1"], g["out"]
+    N, H, W, C = x.shape
+    Co = w.shape[0]
+    sc = [(3 + i, "u32", v) for i, v in enumerate((N, H, W, C, Co, 3, 3, 1))]
+    m, o = _manifest_for(tmp_path, "conv2d_f32", [x, w], want.shape, sc)
+    got = _run_manifest(host, m, o, want.shape)
+    assert np.all(np.abs(got - want) <= 1e-3 + 1e-3 * np.abs(want))
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((8, 64, 64, 64), dtype=np.float32)
+    w = rng.standard_normal((128, 3, 3, 64), dtype=np.float32)
+    sc = [(3 + i, "u32", v) for i, v in enumerate((8, 64, 64, 64, 128, 3, 3, 1))]
+    m, o = _manifest_for(tmp_path, "conv2d_f32", [x, w], (8, 62, 62, 128), sc)
+    got = _run_manifest(host, m, o, (8, 62, 62, 128))
+    want = O.conv2d_nhwc(x, w, padding=0, acc=np.float64)
+    assert np.all(np.abs(got - want) <= 1e-3 + 1e-3 * np.abs(want))
+
+
+@pytest.mark.gpu
+def test_host_runs_reference_llama_decoder_f32_manifest(host, tmp_path):
+    """The reference's llama_decoder_layer entry (full/registry.py:87-104):
+    fp32, S 64, D 128, H 4 / H_kv 2 (head_dim 32), FF 256, rtol = atol = 1e-2
+    on every element against the golden the reference hook produced."""
+    g = np.load(REPO / "tests" / "golden" / "llama_decoder_layer.npz")
+    ins = [g[f"in{i}"] for i in range(5)]
+    want = g["out"]
+    sc = [(6, "u32", 64), (7, "u32", 128), (8, "u32", 4), (9, "u32", 2), (10, "u32", 256),
+          (11, "f32", 10000.0), (12, "f32", 1e-5)]
+    m, o = _manifest_for(tmp_path, "llama_decoder_layer_f32", ins, want.shape, sc)
+    got = _run_manifest(host, m, o, want.shape)
+    assert np.all(np.abs(got - want) <= 1e-2 + 1e-2 * np.abs(want)), np.abs(got - want).max()

@@ -45,6 +45,8 @@ def test_link_md_links_b200_kernels_to_their_cuda_sources(tmp_path):
 
 def test_kernels_for_maps_changes_to_registry_names():
     assert lb.kernels_for(["metalbench_b200/csrc/conv2d.cu"]) == ["conv2d"]
+    assert lb.kernels_for(["metalbench_b200/csrc/f32_paths.cu"]) == ["conv2d_f32",
+                                                                      "llama_decoder_layer_f32"]
     assert "swiglu" in lb.kernels_for(["mlx/kernels/standard/swiglu.py"])
     assert {"sqr_mm", "rect_mm", "batch_mm"} <= set(lb.kernels_for(["metalbench_b200/csrc/gemm.cu"]))
     from metalbench_b200 import harness
