@@ -245,14 +245,30 @@ int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, 
                              int max_pages, int causal, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* mb_decoder_layer_forward with the residual stream kept in fp32 between
+ * layers (a stack of layers hands it on): x_res32 [B*S, D] fp32 is the layer
+ * input's residual (x must hold its bf16 rounding; null = use x), and when
+ * y_res32 is not null it receives the fp32 output beside the bf16 y. Inside
+ * the layer the residual adds are fp32 in either case; under tensor
+ * parallelism the ranks' partial products are all-reduced in bf16 and the
+ * residual is added after the reduction. Same reference as
+ * mb_decoder_layer_forward (mlx/kernels/full/llama_decoder_layer.py:24-46,
+ * whose x stays fp32 throughout). */
+int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x, const float* x_res32,
+                                uint16_t* y, float* y_res32, int B, int S, const int* start_pos,
+                                const int* kv_len, int max_kv_len, uint16_t* k_cache,
+                                uint16_t* v_cache, const int* block_table, int max_pages,
+                                int causal, void* workspace, size_t workspace_bytes, void* stream);
+
 /* fp32 decoder layer for the reference's own llama_decoder_layer_f32 entry
  * (mlx/kernels/full/llama_decoder_layer.py:24-64; registry
  * mlx/kernels/full/registry.py:87-104: S 64, D 128, H 4 / H_kv 2, head_dim 32,
  * FF 256, rtol = atol = 1e-2). x, y [B*S, D] fp32; weights fp32 in the
  * reference (in, out) layout; head_dim = D/H even and <= 256, D and FF
  * multiples of 4. Every sequence's tokens sit at positions 0..S-1; causal = 0
- * is the reference hook. GEMMs run in 3xTF32 (fp32-accurate); norms, RoPE,
- * softmax and SwiGLU in fp32. Scratch: mb_llama_decoder_f32_workspace_bytes,
+ * is the reference hook. Everything runs in fp32 (the GEMMs as fp32 FMA
+ * tiles: with N(0,1) weights the softmax is nearly one-hot and magnifies any
+ * product error). Scratch: mb_llama_decoder_f32_workspace_bytes,
  * 256-byte aligned, caller owned. */
 size_t mb_llama_decoder_f32_workspace_bytes(int B, int S, int D, int H, int H_kv, int FF);
 int mb_llama_decoder_f32(const float* x, const float* W_qkv, const float* W_o, const float* W_gu,

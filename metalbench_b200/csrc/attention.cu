@@ -32,23 +32,32 @@ __device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float(((uin
 __device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// out[b, (kvh*G+g)*DH + d] = sum_split o * 2^(m - M) / sum_split l * 2^(m - M)
+// Decode partials: every (CTA, unit) segment of the flattened page range has
+// pps (max, sum, o) triples per query head -- one per warp (pps = 4), or one
+// merged over the warps (pps = 1) -- at
+//   part_ml[((unit*smax + j)*pps + w)*G + g][0..1], part_o[...][0..DH-1],
+// j = CTA index - first CTA of the unit. The combine merges the segments of
+// its unit: out = sum o * 2^(m - M) / sum l * 2^(m - M).
 __global__ void attn_combine_kernel(const float* __restrict__ part_o,
-                                    const float* __restrict__ part_ml, int splits, int G, int Hkv,
-                                    uint16_t* __restrict__ out, int ldo) {
+                                    const float* __restrict__ part_ml, int pages, int per,
+                                    int smax, int pps, int G, int Hkv, uint16_t* __restrict__ out,
+                                    int ldo) {
   mbd::pdl_trigger();
   mbd::pdl_wait();
   const int g = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
-  const int64_t base = ((int64_t)b * Hkv + kvh) * splits;
+  const int64_t unit = (int64_t)b * Hkv + kvh;
+  const int64_t c0 = unit * pages / per, c1 = (unit * pages + pages - 1) / per;
+  const int nparts = (int)(c1 - c0 + 1) * pps;
+  const int64_t base = unit * smax * pps;
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, part_ml[((base + s) * G + g) * 2]);
+  for (int i = 0; i < nparts; ++i) M = fmaxf(M, part_ml[((base + i) * G + g) * 2]);
   float Ls = 0.f, acc = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float m = part_ml[((base + s) * G + g) * 2];
+  for (int i = 0; i < nparts; ++i) {
+    const float m = part_ml[((base + i) * G + g) * 2];
     if (m == -INFINITY) continue;
     const float c = exp2f(m - M);
-    Ls += part_ml[((base + s) * G + g) * 2 + 1] * c;
-    acc += part_o[((base + s) * G + g) * DH + d] * c;
+    Ls += part_ml[((base + i) * G + g) * 2 + 1] * c;
+    acc += part_o[((base + i) * G + g) * DH + d] * c;
   }
   const float r = Ls > 0.f ? acc / Ls : 0.f;
   __nv_bfloat16 h = __float2bfloat16_rn(r);
@@ -281,154 +290,219 @@ namespace {
 
 // ---------------------------------------------------------------------------
 // decode on the warp MMA: the G query heads of one kv head are the 16 MMA rows
-// (rows >= G are zero). grid (splits, Hkv, B), 128 threads. Pages of the
-// split's key range are staged whole (K and V, 16 KiB each) into a
-// three-deep cp.async ring; warp w takes keys 16w..16w+15 of every page and
-// keeps its own online-softmax state; the four warps are merged at the end and
-// one (max, sum, o) partial per split goes to the combine kernel.
+// (rows >= G are zero). The work is the flat list of (unit, page) pairs,
+// unit = (sequence, kv head), each unit `pages` long (pages past a sequence's
+// kv_len are skipped); CTA c streams pairs c*per .. (c+1)*per-1. With few
+// units (tensor parallel) the ranges cross unit boundaries, so every SM gets
+// the same number of pages in one resident wave; with many, they are
+// unit-aligned splits (decode_plan).
+// Pages are staged whole (K and V, 16 KiB each) into a three-deep cp.async
+// ring; warp w takes keys 16w..16w+15 of every page with its own
+// online-softmax state, which it writes out as a partial whenever the unit
+// changes (and at the end); attn_combine_kernel merges the partials.
 // ---------------------------------------------------------------------------
 constexpr int DEC_STAGES = 3;
 
 __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
     const uint16_t* __restrict__ q, int ldq, const uint16_t* __restrict__ kc,
     const uint16_t* __restrict__ vc, const int* __restrict__ block_table, int max_pages,
-    const int* __restrict__ kv_len, int Hkv, int G, int pages_per_split, float scale_log2,
-    float* __restrict__ part_o, float* __restrict__ part_ml) {
+    const int* __restrict__ kv_len, int Hkv, int G, int pages, int per, int64_t total, int smax,
+    int merged, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml) {
   mbd::pdl_trigger();
   mbd::pdl_wait();
   extern __shared__ __align__(16) uint16_t sm[];
   uint16_t* Ks = sm;                                // [STAGES][64][KV_LD]
   uint16_t* Vs = sm + DEC_STAGES * PAGE * KV_LD;    // [STAGES][64][KV_LD]
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, splits = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int L = kv_len[b];
-  const int pg_begin = split * pages_per_split;
-  const int pg_end = min((L + PAGE - 1) / PAGE, pg_begin + pages_per_split);
-  const int npg = max(0, pg_end - pg_begin);
+  const int64_t begin = (int64_t)blockIdx.x * per;
+  const int64_t endp = begin + per < total ? begin + per : total;
+  const int n = (int)(endp - begin);
 
-  uint32_t qa[8][4];
-  {
-    const uint16_t* qr = q + (int64_t)b * ldq + (kvh * G) * DH;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int c = ks * 16 + tig * 2;
-      const bool ra = gid < G, rb = gid + 8 < G;
-      qa[ks][0] = ra ? *reinterpret_cast<const uint32_t*>(qr + gid * DH + c) : 0u;
-      qa[ks][1] = rb ? *reinterpret_cast<const uint32_t*>(qr + (gid + 8) * DH + c) : 0u;
-      qa[ks][2] = ra ? *reinterpret_cast<const uint32_t*>(qr + gid * DH + c + 8) : 0u;
-      qa[ks][3] = rb ? *reinterpret_cast<const uint32_t*>(qr + (gid + 8) * DH + c + 8) : 0u;
+  // Pages are loaded and consumed in order: both sides step a (unit, page)
+  // cursor instead of dividing the flat index.
+  const int64_t units = total / pages;
+  int ld_u = (int)(begin / pages), ld_kt = (int)(begin - (int64_t)ld_u * pages);
+  int ld_b = ld_u / Hkv, ld_L = kv_len[ld_b];
+  auto load_next = [&](int buf) {
+    if (ld_kt * PAGE < ld_L) {  // else nothing of this page is attended
+      const int kvh = ld_u - ld_b * Hkv;
+      const int pg = block_table[ld_b * max_pages + ld_kt];
+      const int64_t base = ((int64_t)pg * Hkv + kvh) * PAGE * DH;
+      for (int c = threadIdx.x; c < PAGE * DH / 8; c += 128) {
+        const int row = c >> 4, col = (c & 15) * 8;
+        const bool ok = ld_kt * PAGE + row < ld_L;
+        cp_async16(Ks + (buf * PAGE + row) * KV_LD + col, kc + base + row * DH + col, ok);
+        cp_async16(Vs + (buf * PAGE + row) * KV_LD + col, vc + base + row * DH + col, ok);
+      }
     }
-  }
-  auto load_page = [&](int i, int buf) {
-    const int kt = pg_begin + i;
-    const int pg = block_table[b * max_pages + kt];
-    const int64_t base = ((int64_t)pg * Hkv + kvh) * PAGE * DH;
-    for (int c = threadIdx.x; c < PAGE * DH / 8; c += 128) {
-      const int row = c >> 4, col = (c & 15) * 8;
-      const bool ok = kt * PAGE + row < L;
-      cp_async16(Ks + (buf * PAGE + row) * KV_LD + col, kc + base + row * DH + col, ok);
-      cp_async16(Vs + (buf * PAGE + row) * KV_LD + col, vc + base + row * DH + col, ok);
+    if (++ld_kt == pages) {
+      ld_kt = 0;
+      if (++ld_u < units) {
+        ld_b = ld_u / Hkv;
+        ld_L = kv_len[ld_b];
+      }
     }
   };
   // prologue: STAGES-1 pages in flight (empty groups keep the counting uniform)
 #pragma unroll
   for (int i = 0; i < DEC_STAGES - 1; ++i) {
-    if (i < npg) load_page(i, i);
+    if (i < n) load_next(i);
     cp_async_commit();
   }
+  uint32_t qa[8][4];
   float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  int cur = -1, cur_b = 0, cur_L = 0;
+  int unit = (int)(begin / pages), kt = (int)(begin - (int64_t)unit * pages);  // consumer cursor
 
-  for (int i = 0; i < npg; ++i) {
-    const int buf = i % DEC_STAGES;
-    if (i + DEC_STAGES - 1 < npg) load_page(i + DEC_STAGES - 1, (i + DEC_STAGES - 1) % DEC_STAGES);
-    cp_async_commit();
-    cp_async_wait<DEC_STAGES - 1>();
-    __syncthreads();
-    const uint16_t* K = Ks + (buf * PAGE + warp * 16) * KV_LD;
-    const uint16_t* V = Vs + (buf * PAGE + warp * 16) * KV_LD;
-    const int key0 = (pg_begin + i) * PAGE + warp * 16;
-    float s[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const uint16_t* kr = K + (nt * 8 + (lane & 7)) * KV_LD + (lane >> 3) * 8;
-#pragma unroll
-      for (int ks = 0; ks < 8; ks += 2) {
-        uint32_t b[4];
-        ldsm_x4(b, kr + ks * 16);
-        mma_bf16_16816(s[nt], qa[ks], b[0], b[1]);
-        mma_bf16_16816(s[nt], qa[ks + 1], b[2], b[3]);
-      }
-    }
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const bool ok = key0 + nt * 8 + tig * 2 + e < L;
-        s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
-        s[nt][2 + e] = ok ? s[nt][2 + e] * scale_log2 : -INFINITY;
-        mx_a = fmaxf(mx_a, s[nt][e]);
-        mx_b = fmaxf(mx_b, s[nt][2 + e]);
-      }
+  // this warp's (max, sum, o) of unit `cur` -> its partial slot; state reset
+  auto flush = [&]() {
+    float la = l_a, lb = l_b;
 #pragma unroll
     for (int off = 1; off <= 2; off <<= 1) {
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+      la += __shfl_xor_sync(0xffffffffu, la, off);
+      lb += __shfl_xor_sync(0xffffffffu, lb, off);
     }
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float sa = mn_a == -INFINITY ? 0.f : mn_a, sb = mn_b == -INFINITY ? 0.f : mn_b;
-    const float ca = exp2f(m_a - sa), cb = exp2f(m_b - sb);
-    m_a = mn_a;
-    m_b = mn_b;
-    float sum_a = 0.f, sum_b = 0.f;
+    const int64_t c0 = (int64_t)cur * pages / per;
+    const int64_t slot = (((int64_t)cur * smax + (blockIdx.x - c0)) * 4 + warp) * G;
+    if (gid < G) {
+      float* po = part_o + (slot + gid) * DH;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = exp2f(s[nt][0] - sa);
-      s[nt][1] = exp2f(s[nt][1] - sa);
-      s[nt][2] = exp2f(s[nt][2] - sb);
-      s[nt][3] = exp2f(s[nt][3] - sb);
-      sum_a += s[nt][0] + s[nt][1];
-      sum_b += s[nt][2] + s[nt][3];
+      for (int dt = 0; dt < 16; ++dt)
+        *reinterpret_cast<float2*>(po + dt * 8 + tig * 2) = make_float2(o[dt][0], o[dt][1]);
+      if (tig == 0) *reinterpret_cast<float2*>(part_ml + (slot + gid) * 2) = make_float2(m_a, la);
     }
-    l_a = l_a * ca + sum_a;
-    l_b = l_b * cb + sum_b;
-    uint32_t pa[4];
-    pa[0] = pack2(s[0][0], s[0][1]);
-    pa[1] = pack2(s[0][2], s[0][3]);
-    pa[2] = pack2(s[1][0], s[1][1]);
-    pa[3] = pack2(s[1][2], s[1][3]);
-    const uint16_t* vr = V + (((lane >> 3) & 1) * 8 + (lane & 7)) * KV_LD + (lane >> 4) * 8;
+    if (gid + 8 < G) {
+      float* po = part_o + (slot + gid + 8) * DH;
 #pragma unroll
-    for (int dt = 0; dt < 16; dt += 2) {
-      o[dt][0] *= ca;
-      o[dt][1] *= ca;
-      o[dt][2] *= cb;
-      o[dt][3] *= cb;
-      o[dt + 1][0] *= ca;
-      o[dt + 1][1] *= ca;
-      o[dt + 1][2] *= cb;
-      o[dt + 1][3] *= cb;
-      uint32_t b[4];
-      ldsm_x4_t(b, vr + dt * 8);
-      mma_bf16_16816(o[dt], pa, b[0], b[1]);
-      mma_bf16_16816(o[dt + 1], pa, b[2], b[3]);
+      for (int dt = 0; dt < 16; ++dt)
+        *reinterpret_cast<float2*>(po + dt * 8 + tig * 2) = make_float2(o[dt][2], o[dt][3]);
+      if (tig == 0)
+        *reinterpret_cast<float2*>(part_ml + (slot + gid + 8) * 2) = make_float2(m_b, lb);
+    }
+  };
+
+  for (int i = 0; i < n; ++i, ++kt) {
+    const int buf = i % DEC_STAGES;
+    if (i + DEC_STAGES - 1 < n) load_next((i + DEC_STAGES - 1) % DEC_STAGES);
+    cp_async_commit();
+    if (kt == pages) {
+      kt = 0;
+      ++unit;
+    }
+    if (unit != cur) {  // a new (sequence, kv head): flush the old one, load q
+      if (cur >= 0) flush();
+      cur = unit;
+      cur_b = unit / Hkv;
+      cur_L = kv_len[cur_b];
+      const int kvh = unit - cur_b * Hkv;
+      const uint16_t* qr = q + (int64_t)cur_b * ldq + (kvh * G) * DH;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int c = ks * 16 + tig * 2;
+        const bool ra = gid < G, rb = gid + 8 < G;
+        qa[ks][0] = ra ? *reinterpret_cast<const uint32_t*>(qr + gid * DH + c) : 0u;
+        qa[ks][1] = rb ? *reinterpret_cast<const uint32_t*>(qr + (gid + 8) * DH + c) : 0u;
+        qa[ks][2] = ra ? *reinterpret_cast<const uint32_t*>(qr + gid * DH + c + 8) : 0u;
+        qa[ks][3] = rb ? *reinterpret_cast<const uint32_t*>(qr + (gid + 8) * DH + c + 8) : 0u;
+      }
+#pragma unroll
+      for (int t = 0; t < 16; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+      m_a = m_b = -INFINITY;
+      l_a = l_b = 0.f;
+    }
+    cp_async_wait<DEC_STAGES - 1>();
+    __syncthreads();
+    const int key0 = kt * PAGE + warp * 16;
+    if (key0 < cur_L) {  // warp-uniform: some of this warp's 16 keys are attended
+      const uint16_t* K = Ks + (buf * PAGE + warp * 16) * KV_LD;
+      const uint16_t* V = Vs + (buf * PAGE + warp * 16) * KV_LD;
+      float s[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+        const uint16_t* kr = K + (nt * 8 + (lane & 7)) * KV_LD + (lane >> 3) * 8;
+#pragma unroll
+        for (int ks = 0; ks < 8; ks += 2) {
+          uint32_t bb[4];
+          ldsm_x4(bb, kr + ks * 16);
+          mma_bf16_16816(s[nt], qa[ks], bb[0], bb[1]);
+          mma_bf16_16816(s[nt], qa[ks + 1], bb[2], bb[3]);
+        }
+      }
+      float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool ok = key0 + nt * 8 + tig * 2 + e < cur_L;
+          s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
+          s[nt][2 + e] = ok ? s[nt][2 + e] * scale_log2 : -INFINITY;
+          mx_a = fmaxf(mx_a, s[nt][e]);
+          mx_b = fmaxf(mx_b, s[nt][2 + e]);
+        }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+      }
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float sa = mn_a == -INFINITY ? 0.f : mn_a, sb = mn_b == -INFINITY ? 0.f : mn_b;
+      const float ca = exp2f(m_a - sa), cb = exp2f(m_b - sb);
+      m_a = mn_a;
+      m_b = mn_b;
+      float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = exp2f(s[nt][0] - sa);
+        s[nt][1] = exp2f(s[nt][1] - sa);
+        s[nt][2] = exp2f(s[nt][2] - sb);
+        s[nt][3] = exp2f(s[nt][3] - sb);
+        sum_a += s[nt][0] + s[nt][1];
+        sum_b += s[nt][2] + s[nt][3];
+      }
+      l_a = l_a * ca + sum_a;
+      l_b = l_b * cb + sum_b;
+      uint32_t pa[4];
+      pa[0] = pack2(s[0][0], s[0][1]);
+      pa[1] = pack2(s[0][2], s[0][3]);
+      pa[2] = pack2(s[1][0], s[1][1]);
+      pa[3] = pack2(s[1][2], s[1][3]);
+      const uint16_t* vr = V + (((lane >> 3) & 1) * 8 + (lane & 7)) * KV_LD + (lane >> 4) * 8;
+#pragma unroll
+      for (int dt = 0; dt < 16; dt += 2) {
+        o[dt][0] *= ca;
+        o[dt][1] *= ca;
+        o[dt][2] *= cb;
+        o[dt][3] *= cb;
+        o[dt + 1][0] *= ca;
+        o[dt + 1][1] *= ca;
+        o[dt + 1][2] *= cb;
+        o[dt + 1][3] *= cb;
+        uint32_t bb[4];
+        ldsm_x4_t(bb, vr + dt * 8);
+        mma_bf16_16816(o[dt], pa, bb[0], bb[1]);
+        mma_bf16_16816(o[dt + 1], pa, bb[2], bb[3]);
+      }
     }
     __syncthreads();  // this buffer is refilled STAGES-1 iterations later
   }
   cp_async_wait<0>();
-  __syncthreads();  // the ring is reused below as the merge area
+  if (cur < 0) return;
+  if (!merged) {
+    flush();
+    return;
+  }
+  // Unit-aligned range: the ring is free now, so the four warps' states are
+  // merged in shared memory and one partial per (unit, split) is written.
+  __syncthreads();
 #pragma unroll
   for (int off = 1; off <= 2; off <<= 1) {
     l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
   }
-  // merge warps: [4 warps][16 rows] m, l then [4][16][DH] o (33 KB < ring)
-  float* red = reinterpret_cast<float*>(sm);
+  float* red = reinterpret_cast<float*>(sm);  // [4][16] m, [4][16] l, [4][16][DH] o
   float* rm = red;
   float* rl = red + 64;
   float* ro = red + 128;
@@ -441,13 +515,13 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
 #pragma unroll
   for (int dt = 0; dt < 16; ++dt) {
     const int d = dt * 8 + tig * 2;
-    ro[(warp * 16 + gid) * DH + d] = o[dt][0];
-    ro[(warp * 16 + gid) * DH + d + 1] = o[dt][1];
-    ro[(warp * 16 + gid + 8) * DH + d] = o[dt][2];
-    ro[(warp * 16 + gid + 8) * DH + d + 1] = o[dt][3];
+    *reinterpret_cast<float2*>(ro + (warp * 16 + gid) * DH + d) = make_float2(o[dt][0], o[dt][1]);
+    *reinterpret_cast<float2*>(ro + (warp * 16 + gid + 8) * DH + d) =
+        make_float2(o[dt][2], o[dt][3]);
   }
   __syncthreads();
-  const int64_t unit = ((int64_t)b * Hkv + kvh) * splits + split;
+  const int64_t c0 = (int64_t)cur * pages / per;
+  const int64_t slot = ((int64_t)cur * smax + (blockIdx.x - c0)) * G;
   for (int idx = threadIdx.x; idx < G * DH; idx += 128) {
     const int g = idx / DH, d = idx % DH;
     float M = -INFINITY;
@@ -459,38 +533,79 @@ __global__ void __launch_bounds__(128) attn_decode_mma_kernel(
       Ls += rl[w * 16 + g] * c;
       acc += ro[(w * 16 + g) * DH + d] * c;
     }
-    part_o[(unit * G + g) * DH + d] = acc;
-    if (d == 0) {
-      part_ml[(unit * G + g) * 2] = M;
-      part_ml[(unit * G + g) * 2 + 1] = Ls;
-    }
+    part_o[(slot + g) * DH + d] = acc;
+    if (d == 0) *reinterpret_cast<float2*>(part_ml + (slot + g) * 2) = make_float2(M, Ls);
   }
 }
 
 }  // namespace
 
 namespace {
-// Pages per split: about 12 CTAs per SM over all (sequence, kv head) units,
-// so the last partial wave is short, but at least 4 pages (64 KiB of K+V) per
-// CTA so the ring has work to overlap.
-int decode_split_pages(int B, int Hkv, int max_kv_len, int* splits) {
-  const int units = B * Hkv;
-  const int pages = (max_kv_len + PAGE - 1) / PAGE;
-  const int want = (12 * mb::num_sms() + units - 1) / units;
-  int pps = (pages + want - 1) / want;
-  if (pps < 4) pps = 4;
-  *splits = (pages + pps - 1) / pps;
-  return pps;
-}
 constexpr int DEC_SMEM = 2 * DEC_STAGES * PAGE * KV_LD * 2;
+
+// Decode plan: `pages` per unit (padded to a multiple of `per` when the CTA
+// ranges are unit-aligned), `per` pages per CTA over the B*Hkv*pages pairs,
+// `smax` = most CTAs one unit can span, grid = CTAs launched.
+struct DecodePlan {
+  int pages, per, smax, grid, merged;
+  int64_t total;
+};
+
+int decode_resident_ctas() {
+  static int per_sm[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!per_sm[dev]) {
+    // the occupancy query sees the dynamic shared memory opt-in, so set it first
+    int nb = 0;
+    if (mb::ensure_smem_attr(reinterpret_cast<const void*>(attn_decode_mma_kernel), DEC_SMEM) ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, attn_decode_mma_kernel, 128,
+                                                      DEC_SMEM) != cudaSuccess || nb < 1)
+      nb = 1;
+    per_sm[dev] = nb;
+  }
+  return per_sm[dev] * mb::num_sms();
+}
+
+DecodePlan decode_plan(int B, int Hkv, int max_kv_len) {
+  DecodePlan p;
+  const int pages = (max_kv_len + PAGE - 1) / PAGE;
+  const int64_t units = (int64_t)B * Hkv;
+  const int64_t slots = decode_resident_ctas();
+  if (units >= slots) {
+    // Enough (sequence, kv head) units to fill the GPU: unit-aligned splits of
+    // at least 4 pages, ~12 CTAs per SM in all. Consecutive CTAs then read the
+    // same page range of neighbouring kv heads, which lie next to each other
+    // in the cache, and the many short waves hide each CTA's ramp.
+    const int64_t want = (12 * (int64_t)mb::num_sms() + units - 1) / units;
+    int pps = (int)((pages + want - 1) / want);
+    if (pps < 4) pps = 4;
+    const int splits = (pages + pps - 1) / pps;
+    p.pages = splits * pps;  // padded: no CTA range crosses a unit
+    p.per = pps;
+    p.merged = 1;
+  } else {
+    // Few units (tensor parallel: B * Hkv/P): one resident wave, each CTA the
+    // same share of the flat page list, crossing unit boundaries.
+    p.pages = pages;
+    int64_t per = (units * pages + slots - 1) / slots;
+    if (per < 2) per = 2;
+    p.per = (int)per;
+    p.merged = 0;
+  }
+  p.total = units * p.pages;
+  p.grid = (int)((p.total + p.per - 1) / p.per);
+  p.smax = (p.pages + p.per - 1) / p.per + 1;
+  return p;
+}
 }  // namespace
 
 extern "C" size_t mb_attention_decode_workspace_bytes(int B, int Hq, int Hkv, int max_kv_len) {
-  if (B <= 0 || Hkv <= 0 || max_kv_len <= 0) return 0;
-  int splits;
-  decode_split_pages(B, Hkv, max_kv_len, &splits);
-  const size_t units = (size_t)B * Hq * splits;
-  return units * DH * 4 + units * 2 * 4 + 256;
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || max_kv_len <= 0) return 0;
+  const DecodePlan p = decode_plan(B, Hkv, max_kv_len);
+  const size_t rows = (size_t)B * Hkv * p.smax * (p.merged ? 1 : 4) * (size_t)(Hq / Hkv);
+  return rows * DH * 4 + rows * 2 * 4 + 256;
 }
 
 extern "C" int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16_t* k_cache,
@@ -504,22 +619,24 @@ extern "C" int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16
   MB_REQUIRE(G <= 16, "attention decode: at most 16 query heads per kv head");
   MB_REQUIRE(max_kv_len > 0 && max_kv_len <= max_pages * PAGE, "attention: bad max_kv_len");
   if (B == 0) return MB_OK;
+  MB_REQUIRE(B <= 65535 && Hkv <= 65535, "attention decode: grid too large");
   const size_t need = mb_attention_decode_workspace_bytes(B, Hq, Hkv, max_kv_len);
   MB_REQUIRE(workspace && workspace_bytes >= need,
              "attention decode: workspace of %zu bytes required", need);
-  int splits;
-  const int pps = decode_split_pages(B, Hkv, max_kv_len, &splits);
-  float* part_o = static_cast<float*>(workspace);
-  float* part_ml = part_o + (size_t)B * Hq * splits * DH;
-  const float scale_log2 = 1.4426950408889634f / sqrtf((float)DH);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = mb::ensure_smem_attr(reinterpret_cast<const void*>(attn_decode_mma_kernel), DEC_SMEM);
   if (rc) return rc;
-  MB_CUDA(mb::launch_pdl(attn_decode_mma_kernel, dim3(splits, Hkv, B), dim3(128), DEC_SMEM, s, q,
-                          ldq, k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, pps,
-                          scale_log2, part_o, part_ml));
+  const DecodePlan p = decode_plan(B, Hkv, max_kv_len);
+  float* part_o = static_cast<float*>(workspace);
+  const int pps = p.merged ? 1 : 4;
+  float* part_ml = part_o + (size_t)B * Hkv * p.smax * pps * G * DH;
+  const float scale_log2 = 1.4426950408889634f / sqrtf((float)DH);
+  MB_CUDA(mb::launch_pdl(attn_decode_mma_kernel, dim3(p.grid), dim3(128), DEC_SMEM, s, q, ldq,
+                          k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, p.pages, p.per,
+                          p.total, p.smax, p.merged, scale_log2, part_o, part_ml));
   MB_CUDA(mb::launch_pdl(attn_combine_kernel, dim3(G, Hkv, B), dim3(DH), 0, s,
-                          (const float*)part_o, (const float*)part_ml, splits, G, Hkv, out, ldo));
+                          (const float*)part_o, (const float*)part_ml, p.pages, p.per, p.smax,
+                          pps, G, Hkv, out, ldo));
   return MB_OK;
 }
 

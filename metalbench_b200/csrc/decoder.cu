@@ -53,6 +53,84 @@ __global__ void rownorm_kernel(const uint16_t* __restrict__ x, int M, int D, flo
   if (lane == 0) rstd[row] = rsqrtf(acc / (float)D + eps);
 }
 
+// Same from an fp32 residual stream (16-byte loads).
+__global__ void rownorm_f32_kernel(const float* __restrict__ x, int M, int D, float eps,
+                                   float* __restrict__ rstd) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4* p = reinterpret_cast<const float4*>(x + (int64_t)row * D);
+  float acc = 0.f;
+  for (int c = lane; c < D / 4; c += 32) {
+    const float4 w = p[c];
+    acc += w.x * w.x + w.y * w.y + w.z * w.z + w.w * w.w;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) rstd[row] = rsqrtf(acc / (float)D + eps);
+}
+
+// Tensor-parallel residual step, one CTA per row: io (bf16) holds the
+// all-reduced sum of the ranks' partial outputs; out32 = residual + io in fp32
+// (residual from res32, else from the bf16 res16), io = bf16(out32), and with
+// rstd_out, rstd_out[row] = rsqrt(mean(out32^2) + eps).
+__global__ void residual_add_kernel(uint16_t* __restrict__ io, const float* __restrict__ res32,
+                                    const uint16_t* __restrict__ res16, float* __restrict__ out32,
+                                    int D, float* __restrict__ rstd_out, float eps) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
+  const int64_t row = blockIdx.x;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+    const int64_t off = row * D + c;
+    const uint4 a = *reinterpret_cast<const uint4*>(io + off);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    float v[8];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      v[2 * m] = __uint_as_float(aw[m] << 16);
+      v[2 * m + 1] = __uint_as_float(aw[m] & 0xFFFF0000u);
+    }
+    if (res32) {
+      const float4 r0 = *reinterpret_cast<const float4*>(res32 + off);
+      const float4 r1 = *reinterpret_cast<const float4*>(res32 + off + 4);
+      v[0] += r0.x; v[1] += r0.y; v[2] += r0.z; v[3] += r0.w;
+      v[4] += r1.x; v[5] += r1.y; v[6] += r1.z; v[7] += r1.w;
+    } else {
+      const uint4 r = *reinterpret_cast<const uint4*>(res16 + off);
+      const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        v[2 * m] += __uint_as_float(rw[m] << 16);
+        v[2 * m + 1] += __uint_as_float(rw[m] & 0xFFFF0000u);
+      }
+    }
+    if (out32) {
+      *reinterpret_cast<float4*>(out32 + off) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(out32 + off + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    *reinterpret_cast<uint4*>(io + off) =
+        make_uint4(gemm::pack_bf16(v[0], v[1]), gemm::pack_bf16(v[2], v[3]),
+                   gemm::pack_bf16(v[4], v[5]), gemm::pack_bf16(v[6], v[7]));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  }
+  if (!rstd_out) return;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  __shared__ float wsum[32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) wsum[w] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) t += wsum[i];
+    rstd_out[row] = rsqrtf(t / (float)D + eps);
+  }
+}
+
 // How the fp32 partial slots of a column are summed: split-K (per <= 0): the
 // same `slots` splits for every column; stream-K (per > 0): column block
 // col/256 was cut into segments by CTAs first..last (first = t*kblocks/per).
@@ -122,7 +200,17 @@ __global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, 
   const float sc = e.row_scale ? e.row_scale[row] * e.alpha : e.alpha;
 #pragma unroll
   for (int j = 0; j < RW; ++j) v[j] *= sc;
-  if (e.residual) {
+  if (e.residual_f32) {
+    const float4* r = reinterpret_cast<const float4*>(e.residual_f32 + (int64_t)row * e.ld_res + col);
+#pragma unroll
+    for (int j = 0; j < RW / 4; ++j) {
+      const float4 t = r[j];
+      v[4 * j] += t.x;
+      v[4 * j + 1] += t.y;
+      v[4 * j + 2] += t.z;
+      v[4 * j + 3] += t.w;
+    }
+  } else if (e.residual) {
     const uint4 w = *reinterpret_cast<const uint4*>(e.residual + (int64_t)row * e.ld_res + col);
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -132,11 +220,13 @@ __global__ void reduce_store_kernel(const float* __restrict__ part, PartSum ps, 
     }
   }
   gemm::store_rowW<RW>(e.out, e.ldo, e.out_f32, row, col, e.N, v);
+  if (e.out_f32_copy) gemm::store_rowW<RW>(e.out_f32_copy, e.ldo, 1, row, col, e.N, v);
   if (!rstd_out) return;
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < RW; ++j) {
-    const float q = __bfloat162float(__float2bfloat16_rn(v[j]));  // the stored value
+    // the norm of the residual stream: fp32 when it is kept, else the stored bf16
+    const float q = e.out_f32_copy ? v[j] : __bfloat162float(__float2bfloat16_rn(v[j]));
     ss += q * q;
   }
 #pragma unroll
@@ -307,7 +397,8 @@ int choose_ksplit(int64_t M, int64_t N, int64_t K) {
 struct Plan {
   int64_t T;
   int ks_qkv, ks_o, ks_gu, ks_down;
-  size_t off_rstd1, off_rstd2, off_q, off_attn, off_x1, off_act, off_part, off_attn_ws, total;
+  size_t off_rstd1, off_rstd2, off_q, off_attn, off_x1, off_x1f, off_act, off_part, off_attn_ws,
+      total;
   size_t attn_ws;
 };
 
@@ -347,6 +438,7 @@ Plan make_plan(const Layer& L, int B, int S, int max_kv_len) {
   p.off_q = o; o += a256(T * L.Dq * 2);
   p.off_attn = o; o += a256(T * L.Dq * 2);
   p.off_x1 = o; o += a256(T * D * 2);
+  p.off_x1f = o; o += a256(T * D * 4);
   p.off_act = o; o += a256(T * L.FF * 2);
   p.off_part = o; o += a256(part);
   p.off_attn_ws = o; o += a256(p.attn_ws);
@@ -470,11 +562,13 @@ extern "C" size_t mb_decoder_layer_workspace_bytes(const void* layer, int B, int
   return make_plan(*static_cast<const Layer*>(layer), B, S, max_kv_len).total;
 }
 
-extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, int B,
-                                        int S, const int* start_pos, const int* kv_len,
-                                        int max_kv_len, uint16_t* k_cache, uint16_t* v_cache,
-                                        const int* block_table, int max_pages, int causal,
-                                        void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
+                                           const float* x_res32, uint16_t* y, float* y_res32,
+                                           int B, int S, const int* start_pos, const int* kv_len,
+                                           int max_kv_len, uint16_t* k_cache, uint16_t* v_cache,
+                                           const int* block_table, int max_pages, int causal,
+                                           void* workspace, size_t workspace_bytes,
+                                           void* stream) {
   MB_REQUIRE(layer && x && y && start_pos && kv_len && k_cache && v_cache && block_table,
              "decoder forward: null argument");
   MB_REQUIRE(B >= 0 && S >= 0, "decoder forward: negative size");
@@ -482,6 +576,8 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   const Layer& L = *static_cast<const Layer*>(layer);
   MB_REQUIRE(max_kv_len >= S && max_kv_len <= max_pages * 64,
              "decoder forward: max_kv_len must be in [S, max_pages*64]");
+  MB_REQUIRE((reinterpret_cast<uintptr_t>(x_res32) | reinterpret_cast<uintptr_t>(y_res32)) % 16 == 0,
+             "decoder forward: fp32 residual buffers must be 16-byte aligned");
   const Plan p = make_plan(L, B, S, max_kv_len);
   MB_REQUIRE(workspace && workspace_bytes >= p.total &&
                  reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
@@ -493,16 +589,22 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   uint16_t* q = reinterpret_cast<uint16_t*>(w + p.off_q);
   uint16_t* attn = reinterpret_cast<uint16_t*>(w + p.off_attn);
   uint16_t* x1 = reinterpret_cast<uint16_t*>(w + p.off_x1);
+  float* x1f = reinterpret_cast<float*>(w + p.off_x1f);  // fp32 residual stream after attention
   uint16_t* act = reinterpret_cast<uint16_t*>(w + p.off_act);
   float* part = reinterpret_cast<float*>(w + p.off_part);
   const int D = L.cfg.d_model, Dh = L.cfg.head_dim;
   const int64_t T = p.T;
   const int Nqkv = L.Dq + 2 * L.Dkv;
+  const bool tp = L.world > 1;
   int rc;
 
-  // 1. rstd1
-  MB_CUDA(mb::launch_pdl(rownorm_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s, x, (int)T,
-                          D, L.cfg.eps, rstd1));
+  // 1. rstd1 (of the fp32 residual stream when the caller keeps one)
+  if (x_res32)
+    MB_CUDA(mb::launch_pdl(rownorm_f32_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
+                            x_res32, (int)T, D, L.cfg.eps, rstd1));
+  else
+    MB_CUDA(mb::launch_pdl(rownorm_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s, x,
+                            (int)T, D, L.cfg.eps, rstd1));
 
   // 2. QKV + RoPE + KV-cache write
   dec::QkvParams qp;
@@ -542,21 +644,29 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
                                    kv_len, B, S, L.Hq, L.Hkv, Dh, causal, attn, L.Dq, s);
   if (rc) return rc;
 
+  // The residual stream is added in fp32 and kept in fp32 (x1f); its bf16
+  // copy x1 is the next GEMM's operand. One GPU: the o-proj epilogue adds
+  // it. Tensor parallel: the ranks' partial products (no residual) are
+  // all-reduced in bf16, then residual_add_kernel adds the fp32 residual.
   bool rstd2_done = false;
-  // 4. x1 = x + attn @ Wo (rank 0 adds the residual; the all-reduce sums shards)
+  // 4. x1 = x + attn @ Wo
   EpiStore eo{};
   eo.M = (int)T;
   eo.N = D;
   eo.out = x1;
   eo.ldo = D;
   eo.alpha = 1.f;
-  eo.residual = L.rank == 0 ? x : nullptr;
   eo.ld_res = D;
+  if (!tp) {
+    eo.residual = x_res32 ? nullptr : x;
+    eo.residual_f32 = x_res32;
+    eo.out_f32_copy = x1f;
+  }
   if (p.ks_o > 1 || use_streamk(T, D)) {
     PartSum ps;
     rc = gemm_partial(attn, L.wo, part, T, D, L.Dq, p.ks_o, s, &ps);
     if (rc) return rc;
-    if (L.world == 1 && D / RW <= 1024) {  // the reduce also yields rstd2 (one CTA per row)
+    if (!tp && D / RW <= 1024) {  // the reduce also yields rstd2 (one CTA per row)
       MB_CUDA(mb::launch_pdl(reduce_store_kernel, dim3((unsigned)T), dim3(D / RW), 0, s, part, ps,
                               (int)T, D, eo, rstd2, L.cfg.eps));
       rstd2_done = true;
@@ -571,15 +681,18 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     if (rc) return rc;
   }
   MB_CUDA(cudaGetLastError());
-  if (L.world > 1) {
+  if (tp) {
     rc = mb::tp_allreduce_sum(x1, (size_t)T * D, s);
     if (rc) return rc;
+    MB_CUDA(mb::launch_pdl(residual_add_kernel, dim3((unsigned)T), dim3(256), 0, s, x1, x_res32,
+                            x, x1f, D, rstd2, L.cfg.eps));
+    rstd2_done = true;
   }
 
-  // 5. rstd2 (unless the o-proj reduce produced it), 6. SwiGLU MLP up
+  // 5. rstd2 (unless produced above), 6. SwiGLU MLP up
   if (!rstd2_done) {
-    MB_CUDA(mb::launch_pdl(rownorm_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
-                            (const uint16_t*)x1, (int)T, D, L.cfg.eps, rstd2));
+    MB_CUDA(mb::launch_pdl(rownorm_f32_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
+                            (const float*)x1f, (int)T, D, L.cfg.eps, rstd2));
   }
   dec::SwigluParams sp;
   sp.M = (int)T;
@@ -608,8 +721,11 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
   ed.out = y;
   ed.ldo = D;
   ed.alpha = 1.f;
-  ed.residual = L.rank == 0 ? x1 : nullptr;
   ed.ld_res = D;
+  if (!tp) {
+    ed.residual_f32 = x1f;
+    ed.out_f32_copy = y_res32;
+  }
   if (p.ks_down > 1 || use_streamk(T, D)) {
     PartSum ps;
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s, &ps);
@@ -623,9 +739,22 @@ extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, ui
     if (rc) return rc;
   }
   MB_CUDA(cudaGetLastError());
-  if (L.world > 1) {
+  if (tp) {
     rc = mb::tp_allreduce_sum(y, (size_t)T * D, s);
     if (rc) return rc;
+    MB_CUDA(mb::launch_pdl(residual_add_kernel, dim3((unsigned)T), dim3(256), 0, s, y,
+                            (const float*)x1f, (const uint16_t*)nullptr, y_res32, D,
+                            (float*)nullptr, 0.f));
   }
   return MB_OK;
+}
+
+extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, int B,
+                                        int S, const int* start_pos, const int* kv_len,
+                                        int max_kv_len, uint16_t* k_cache, uint16_t* v_cache,
+                                        const int* block_table, int max_pages, int causal,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  return mb_decoder_layer_forward_ex(layer, x, nullptr, y, nullptr, B, S, start_pos, kv_len,
+                                     max_kv_len, k_cache, v_cache, block_table, max_pages, causal,
+                                     workspace, workspace_bytes, stream);
 }

@@ -106,6 +106,11 @@ struct EpiStore {
   const uint16_t* residual;  // bf16 [M, ld_res]
   int64_t ld_res;
   int act;  // 0: none; 1: exact GELU x*Phi(x), applied after the scale, before the residual
+  // fp32 residual stream (optional): residual_f32 [M, ld_res] is added instead
+  // of the bf16 residual, and out_f32_copy [M, ldo] receives the fp32 result
+  // beside the (bf16) out.
+  const float* residual_f32;
+  float* out_f32_copy;
   // Scale, add the residual and store 32 accumulator values of row c.row
   // starting at column n.
   __device__ void finish32(const EpiCtx& c, float sc, int n, float (&v)[32]) const {
@@ -115,7 +120,12 @@ struct EpiStore {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.70710678118654752f));
     }
-    if (residual) {
+    if (residual_f32) {
+      const float* r = residual_f32 + (int64_t)c.row * ld_res + n;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n + j < N) v[j] += r[j];
+    } else if (residual) {
       const uint16_t* r = residual + (int64_t)c.row * ld_res + n;
       if (n + 32 <= N && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
 #pragma unroll
@@ -135,6 +145,7 @@ struct EpiStore {
       }
     }
     store_row32(out, ldo, out_f32, c.row, n, N, v);
+    if (out_f32_copy) store_row32(out_f32_copy, ldo, 1, c.row, n, N, v);
   }
   __device__ float scale(const EpiCtx& c) const {
     return (c.row_ok && row_scale) ? row_scale[c.row] * alpha : alpha;

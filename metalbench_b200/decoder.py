@@ -102,12 +102,17 @@ class DecoderLayer:
 
     def forward(self, x: torch.Tensor, cache: PagedKVCache, start_pos: torch.Tensor,
                 causal: bool = True, out: torch.Tensor | None = None,
-                max_kv_len: int | None = None, kv_len: torch.Tensor | None = None) -> torch.Tensor:
+                max_kv_len: int | None = None, kv_len: torch.Tensor | None = None,
+                x_res32: torch.Tensor | None = None,
+                y_res32: torch.Tensor | None = None) -> torch.Tensor:
         """x: [B, S, D] bf16 (or [S, D] for B = 1); start_pos: int32 [B] on the device.
 
         The new tokens' keys/values are appended at start_pos[b].. and attention
         reads positions 0..start_pos[b]+S-1. kv_len (= start_pos + S, int32 on
-        the device) may be passed in when several layers share it."""
+        the device) may be passed in when several layers share it. x_res32 /
+        y_res32 (fp32, x's shape) carry the residual stream in fp32 between
+        layers: x_res32 is this layer's input residual (x its bf16 rounding),
+        y_res32 receives the fp32 output."""
         squeeze = x.dim() == 2
         X = x.unsqueeze(0) if squeeze else x
         ops._cuda(X, "DecoderLayer.forward(x)", (torch.bfloat16,))
@@ -123,7 +128,14 @@ class DecoderLayer:
         ws_bytes = self.workspace_bytes(B, S, max_kv_len)
         ws = ops._workspace(ws_bytes, X.device)
         self._kv_len = kv_len  # keep alive until the stream has consumed it
-        _lib.call("mb_decoder_layer_forward", self._h, X.data_ptr(), out.data_ptr(), B, S,
+        for nm, t in (("x_res32", x_res32), ("y_res32", y_res32)):
+            if t is not None:
+                ops._cuda(t, f"DecoderLayer.forward({nm})", (torch.float32,))
+                if t.numel() != X.numel():
+                    raise ValueError(f"{nm} must have x's shape")
+        _lib.call("mb_decoder_layer_forward_ex", self._h, X.data_ptr(),
+                  0 if x_res32 is None else x_res32.data_ptr(), out.data_ptr(),
+                  0 if y_res32 is None else y_res32.data_ptr(), B, S,
                   start_pos.data_ptr(), kv_len.data_ptr(), max_kv_len, cache.k.data_ptr(),
                   cache.v.data_ptr(), cache.block_table.data_ptr(), cache.max_pages,
                   1 if causal else 0, ws.data_ptr(), ws_bytes, ops._stream())

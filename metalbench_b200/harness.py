@@ -261,7 +261,7 @@ def compare(actual: np.ndarray, expected: np.ndarray, rtol: float, atol: float) 
     nan = bool(np.isnan(a).any())
     return {"all_within": bool(ok.all()), "frac_within_tol": frac,
             "max_err": float(np.nanmax(diff)), "correct": bool(ok.all()),
-            "gate_99": frac >= need,
+            "gate_99": frac >= need, "err_std": float(np.nanstd(a - b)),
             "atol_needed": float("inf") if nan else float(max(0.0, (diff - rtol * np.abs(b)).max()))}
 
 
@@ -302,6 +302,7 @@ def evaluate(name: str, *, seed=None, warmup=10, iters=200, solo=None, ref_warmu
         got = bf16_bits_to_f32(out) if sp["output_dtype"] == "bf16" else out.astype(np.float32)
         cmp = compare(got, ref.reshape(got.shape), b.rtol, b.atol)
         outputs.append(dict(binding=len(sp["input_bindings"]), **cmp))
+        result["ref_abs_max"] = float(np.abs(ref).max()) if ref.size else 0.0
         correct = cmp["correct"]
     t_main = k_t if k_t is not None else r_t
     sec = t_main["median_ms"] / 1000.0

@@ -3,8 +3,9 @@
 Megatron-style sharding inside every layer (libmb200 packs each rank's shard):
 q/k/v heads and gate/up features are split by column, o-proj and down-proj by
 row, and their two partial outputs per layer are summed by an NCCL all-reduce
-over NVLink inside ``mb_decoder_layer_forward``. The KV cache holds only this
-rank's kv heads. A decode step (one new token for each of B sequences
+over NVLink inside ``mb_decoder_layer_forward_ex``; the residual stream is
+handed from layer to layer in fp32. The KV cache holds only this rank's kv
+heads. A decode step (one new token for each of B sequences
 through every layer) can be captured once in a CUDA graph and replayed.
 """
 from __future__ import annotations
@@ -80,9 +81,18 @@ class DecoderStack:
         # one kv_len for all layers: no extra kernel between two layers' launches
         S = x.shape[-2] if x.dim() == 3 else x.shape[0]
         self._kv_len = (start_pos + S).contiguous()
-        for layer, cache in zip(self.layers, self.caches):
+        # the residual stream stays fp32 from layer to layer (two ping-pong
+        # buffers); each layer also emits the bf16 copy the next one's GEMMs read
+        key = tuple(x.shape)
+        if getattr(self, "_res_key", None) != key:
+            self._res = [torch.empty(key, dtype=torch.float32, device=x.device) for _ in range(2)]
+            self._res_key = key
+        res = None
+        for i, (layer, cache) in enumerate(zip(self.layers, self.caches)):
+            nxt = self._res[i % 2]
             x = layer(x, cache, start_pos, causal=causal, max_kv_len=kv_len_max,
-                      kv_len=self._kv_len)
+                      kv_len=self._kv_len, x_res32=res, y_res32=nxt)
+            res = nxt
         return x
 
     # ---- decode step in a CUDA graph ---------------------------------------

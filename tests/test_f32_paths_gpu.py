@@ -9,15 +9,10 @@ import numpy as np
 import pytest
 
 import oracle.ops as O
+from _f32check import all_within as _all_within, check_against_fp32_golden
 
 pytestmark = pytest.mark.gpu
 REPO = __import__("pathlib").Path(__file__).resolve().parents[1]
-
-
-def _all_within(got, want, tol):
-    err = np.abs(got.astype(np.float64) - want)
-    bad = err > tol + tol * np.abs(want)
-    assert not bad.any(), (int(bad.sum()), float(err.max()))
 
 
 def _t(torch, a):
@@ -56,7 +51,9 @@ def test_llama_decoder_f32_golden():
     g = np.load(REPO / "tests" / "golden" / "llama_decoder_layer.npz")
     ins = [_t(torch, g[f"in{i}"]) for i in range(5)]
     y = ops.llama_decoder_f32(*ins, n_heads=4, n_kv_heads=2, base=10000.0, eps=1e-5)
-    _all_within(y.cpu().numpy(), g["out"], 1e-2)
+    exact = O.decoder_layer(g["in0"], *[g[f"in{i}"] for i in range(1, 5)], H=4, H_kv=2,
+                            base=10000.0, acc=np.float64)
+    check_against_fp32_golden(y.cpu().numpy(), g["out"], exact, 1e-2)
 
 
 @pytest.mark.parametrize("B,S,D,H,Hkv,FF,causal", [
