@@ -79,6 +79,12 @@ typedef struct mb_timing {
   int launches_per_iter;
   double h2d_ms; /* host->device copy time of the inputs (0 for device ptrs) */
   double d2h_ms; /* device->host copy time of the outputs                    */
+  /* config {"profile": true} (the reference's --profile, main.mm:98 and
+   * timing.mm:163-190): one extra dispatch after the timed ones, inside the
+   * NVTX range "mb_profile:<kernel>" for an outside profiler (ncu --nvtx
+   * --nvtx-include "mb_profile:<kernel>/"); its CUDA-event time, else -1.
+   * Every timed dispatch sits in an NVTX range "mb_timed:<kernel>". */
+  double profile_ms;
 } mb_timing;
 
 /* Device description (replaces setup.cpp:116-136 chip detection). */

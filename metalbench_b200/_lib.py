@@ -33,7 +33,8 @@ class MbScalar(C.Structure):
 class MbTiming(C.Structure):
     _fields_ = [("min_ms", C.c_double), ("median_ms", C.c_double), ("mean_ms", C.c_double),
                 ("iters", C.c_int), ("smem_bytes", C.c_int), ("threads_per_cta", C.c_int),
-                ("launches_per_iter", C.c_int), ("h2d_ms", C.c_double), ("d2h_ms", C.c_double)]
+                ("launches_per_iter", C.c_int), ("h2d_ms", C.c_double), ("d2h_ms", C.c_double),
+                ("profile_ms", C.c_double)]
 
 
 class MbDevice(C.Structure):

@@ -38,27 +38,51 @@ __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 
 //   part_ml[((unit*smax + j)*pps + w)*G + g][0..1], part_o[...][0..DH-1],
 // j = CTA index - first CTA of the unit. The combine merges the segments of
 // its unit: out = sum o * 2^(m - M) / sum l * 2^(m - M).
-__global__ void attn_combine_kernel(const float* __restrict__ part_o,
-                                    const float* __restrict__ part_ml, int pages, int per,
-                                    int smax, int pps, int G, int Hkv, uint16_t* __restrict__ out,
-                                    int ldo) {
+__global__ void __launch_bounds__(128) attn_combine_kernel(
+    const float* __restrict__ part_o, const float* __restrict__ part_ml, int pages, int per,
+    int smax, int pps, int G, int Hkv, uint16_t* __restrict__ out, int ldo) {
   mbd::pdl_trigger();
   mbd::pdl_wait();
+  extern __shared__ float wsh[];  // one weight per partial
+  __shared__ float red[4];
   const int g = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t unit = (int64_t)b * Hkv + kvh;
   const int64_t c0 = unit * pages / per, c1 = (unit * pages + pages - 1) / per;
   const int nparts = (int)(c1 - c0 + 1) * pps;
   const int64_t base = unit * smax * pps;
+  // all partials' (max, sum) at once, one per thread, then block reductions
   float M = -INFINITY;
-  for (int i = 0; i < nparts; ++i) M = fmaxf(M, part_ml[((base + i) * G + g) * 2]);
-  float Ls = 0.f, acc = 0.f;
-  for (int i = 0; i < nparts; ++i) {
-    const float m = part_ml[((base + i) * G + g) * 2];
-    if (m == -INFINITY) continue;
-    const float c = exp2f(m - M);
-    Ls += part_ml[((base + i) * G + g) * 2 + 1] * c;
-    acc += part_o[((base + i) * G + g) * DH + d] * c;
+  for (int i = threadIdx.x; i < nparts; i += 128) M = fmaxf(M, part_ml[((base + i) * G + g) * 2]);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float Ls = 0.f;
+  for (int i = threadIdx.x; i < nparts; i += 128) {
+    const float2 ml = *reinterpret_cast<const float2*>(part_ml + ((base + i) * G + g) * 2);
+    const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+    wsh[i] = w;
+    Ls += ml.y * w;
   }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, off);
+  if (lane == 0) red[warp] = Ls;
+  __syncthreads();
+  Ls = red[0] + red[1] + red[2] + red[3];
+  // o: thread d sums its column over the partials, loads four at a time
+  float acc = 0.f;
+  int i = 0;
+  for (; i + 4 <= nparts; i += 4) {
+    float t[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = part_o[((base + i + j) * G + g) * DH + d];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc += t[j] * wsh[i + j];
+  }
+  for (; i < nparts; ++i) acc += part_o[((base + i) * G + g) * DH + d] * wsh[i];
   const float r = Ls > 0.f ? acc / Ls : 0.f;
   __nv_bfloat16 h = __float2bfloat16_rn(r);
   out[(int64_t)b * ldo + (kvh * G + g) * DH + d] = *reinterpret_cast<uint16_t*>(&h);
@@ -634,7 +658,9 @@ extern "C" int mb_attention_decode_bf16(const uint16_t* q, int ldq, const uint16
   MB_CUDA(mb::launch_pdl(attn_decode_mma_kernel, dim3(p.grid), dim3(128), DEC_SMEM, s, q, ldq,
                           k_cache, v_cache, block_table, max_pages, kv_len, Hkv, G, p.pages, p.per,
                           p.total, p.smax, p.merged, scale_log2, part_o, part_ml));
-  MB_CUDA(mb::launch_pdl(attn_combine_kernel, dim3(G, Hkv, B), dim3(DH), 0, s,
+  const size_t comb_smem = (size_t)p.smax * pps * sizeof(float);
+  MB_REQUIRE(comb_smem <= 48 * 1024, "attention decode: too many partials per unit");
+  MB_CUDA(mb::launch_pdl(attn_combine_kernel, dim3(G, Hkv, B), dim3(DH), comb_smem, s,
                           (const float*)part_o, (const float*)part_ml, p.pages, p.per, p.smax,
                           pps, G, Hkv, out, ldo));
   return MB_OK;

@@ -33,7 +33,7 @@ from pathlib import Path
 import numpy as np
 
 from . import _lib
-from . import roofline
+from . import clocks, roofline
 
 REPO_ROOT = Path(__file__).resolve().parents[1]
 HOOK_ROOT = REPO_ROOT / "mlx" / "kernels"
@@ -187,7 +187,7 @@ class Baseline:
 # native dispatch (replaces _run_host + metal/scripts/main.mm)
 # ---------------------------------------------------------------------------
 def run_kernel(b: Baseline, inputs: list[np.ndarray], warmup: int, iters: int,
-               flush_l2: bool = False):
+               flush_l2: bool = False, profile: bool = False):
     """mb_run with host buffers: inputs uploaded, output copied back. Returns
     (timing dict in the reference's host JSON shape, output array)."""
     sp = b.spec
@@ -215,14 +215,28 @@ def run_kernel(b: Baseline, inputs: list[np.ndarray], warmup: int, iters: int,
     cfg = dict(sp.get("config", {}))
     if flush_l2:
         cfg["flush_l2"] = True
+    if profile:
+        cfg["profile"] = True
     t = _lib.MbTiming()
-    _lib.call("mb_init", int(os.environ.get("LOCAL_RANK", "0")), 0, 1, None, 0)
-    _lib.call("mb_run", sp["kernel"].encode(), bufs, len(inputs) + 1, sc, len(scal),
-              json.dumps(cfg).encode(), warmup, iters, C.byref(t))
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    _lib.call("mb_init", dev, 0, 1, None, 0)
+    # SM clocks and throttle reasons sampled (NVML, read only) while mb_run
+    # runs: a per-kernel number counts only with its clock record
+    sampler = clocks.NvmlSampler(dev)
+    sampler.start()
+    try:
+        _lib.call("mb_run", sp["kernel"].encode(), bufs, len(inputs) + 1, sc, len(scal),
+                  json.dumps(cfg).encode(), warmup, iters, C.byref(t))
+    finally:
+        sampler.stop()
     timing = {"min_ms": t.min_ms, "median_ms": t.median_ms, "mean_ms": t.mean_ms,
               "iters": t.iters, "h2d_ms": t.h2d_ms, "d2h_ms": t.d2h_ms}
     extra = {"tg_static_mem_bytes": t.smem_bytes, "pso_max_threads_per_tg": t.threads_per_cta,
-             "metal_device": None}
+             "metal_device": None, "clocks": sampler.summary(),
+             "profiling": {"counters_available": False, "enabled": bool(profile),
+                           "profile_ms": t.profile_ms if profile else None,
+                           "nvtx_range": f"mb_profile:{sp['kernel']}",
+                           "timed_nvtx_range": f"mb_timed:{sp['kernel']}"}}
     return timing, extra, out
 
 
@@ -266,7 +280,7 @@ def compare(actual: np.ndarray, expected: np.ndarray, rtol: float, atol: float) 
 
 
 def evaluate(name: str, *, seed=None, warmup=10, iters=200, solo=None, ref_warmup=None,
-             ref_iters=None, flush_l2=False):
+             ref_iters=None, flush_l2=False, profile=False):
     b = Baseline(name)
     sp = b.spec
     inputs = b.make_inputs(seed)
@@ -280,7 +294,7 @@ def evaluate(name: str, *, seed=None, warmup=10, iters=200, solo=None, ref_warmu
 
     k_t = extra = out = None
     if solo != "mlx":
-        k_t, extra, out = run_kernel(b, inputs, warmup, iters, flush_l2=flush_l2)
+        k_t, extra, out = run_kernel(b, inputs, warmup, iters, flush_l2=flush_l2, profile=profile)
         result.update(extra)
         result["kernel_timing"] = k_t
     r_t = ref = None
@@ -367,6 +381,8 @@ def update_session(name: str, result: dict, target: str, iters: int):
     run with the CUDA source that produced it (harness.py:196-247)."""
     if not result.get("correct"):
         return False, "skipped (incorrect)"
+    if (result.get("clocks") or {}).get("rejected"):
+        return False, "skipped (clock record rejected: throttled or clocks pinned low)"
     bucket = result["chip"]["bucket"]
     new_ms = result["kernel_timing"]["median_ms"]
     session = {}
@@ -391,6 +407,7 @@ def update_session(name: str, result: dict, target: str, iters: int):
         "frac_within_tol": min((o["frac_within_tol"] for o in result["outputs"]), default=1.0),
         "roofline_sol": result.get("roofline", {}).get("sol"),
         "reference_impl": result.get("reference_impl"),
+        "clocks": result.get("clocks"),
         "metal_source_path": rel, "metal_source": text, "git_sha": git_sha(),
         "updated_at": _dt.datetime.now(_dt.timezone.utc).isoformat(timespec="seconds"),
     }
@@ -441,6 +458,18 @@ def print_report(result: dict, target: str, score: float) -> None:
     print(f"  stability   : {m['stability']:.2f}  (1.0 = perfectly consistent)")
     if "roofline" in result:
         print(roofline.format_line(result["roofline"]))
+    ck = result.get("clocks")
+    if ck:
+        verdict = ("REJECTED (throttled or clocks pinned low)" if ck.get("rejected")
+                   else "ok" if ck.get("rejected") is False else "no samples")
+        sm = f"{ck['sm_mhz']:.0f}" if ck.get("sm_mhz") else "?"
+        print(f"  clocks      : SM {sm} / {ck.get('sm_max_mhz') or 0:.0f} MHz  "
+              f"reasons={','.join(ck.get('reasons', [])) or '-'}  n={ck.get('samples', 0)}  "
+              f"[{verdict}]")
+    pf = result.get("profiling", {})
+    if pf.get("enabled"):
+        print(f"  profile     : 1 extra dispatch {pf.get('profile_ms', 0):.3f} ms in NVTX range "
+              f"'{pf['nvtx_range']}' (ncu --nvtx --nvtx-include \"{pf['nvtx_range']}/\")")
     if not solo:
         print()
         print(f"  {'target':>10s}   {'score':>10s}")
@@ -469,6 +498,8 @@ def main(argv=None) -> int:
     ap.add_argument("--ref-warmup", type=int, default=None)
     ap.add_argument("--ref-iters", type=int, default=None)
     ap.add_argument("--flush-l2", action="store_true", help="write 2x L2 between timed launches")
+    ap.add_argument("--profile", action="store_true",
+                    help="one extra dispatch inside an NVTX range for an outside profiler (ncu)")
     ap.add_argument("--save", action="store_true")
     ap.add_argument("--no-session", action="store_true")
     ap.add_argument("--target", default="speed", choices=list(TARGETS))
@@ -488,7 +519,7 @@ def main(argv=None) -> int:
     solo_mode = "mlx" if args.mlx_only else ("metal" if args.metal_only else None)
     result = evaluate(args.name, seed=args.seed, warmup=args.warmup, iters=args.iters,
                       solo=solo_mode, ref_warmup=args.ref_warmup, ref_iters=args.ref_iters,
-                      flush_l2=args.flush_l2)
+                      flush_l2=args.flush_l2, profile=args.profile)
     score = grade(result["metrics"], args.target)
     result["target"], result["score"] = args.target, score
     print(f"[chip] {result['chip']['type']:>8s}  '{result['chip']['name']}'  "

@@ -299,6 +299,14 @@ int main(int argc, char** argv) {
   const int warmup = w ? (int)w->n : 10, iters = it ? (int)it->n : 100;
   std::string cfg = "{}";
   if (const J* c = m.get("config")) cfg = dump(*c);
+  const J* prof = m.get("profile");
+  const bool profile = prof && (prof->t == J::BOOL ? prof->b : prof->n != 0);
+  if (profile) {  // the manifest's profile flag rides in the config object
+    if (cfg.size() > 2)
+      cfg = cfg.substr(0, cfg.size() - 1) + ",\"profile\":true}";
+    else
+      cfg = "{\"profile\":true}";
+  }
   fprintf(stderr, "[host] kernel `%s` | setup complete\n", kernel.c_str());
 
   mb_timing t;
@@ -320,10 +328,12 @@ int main(int argc, char** argv) {
       "\"gpu_cores\":%d,\"ram_bytes\":%llu},\"metal_device\":\"%s\",\"device\":\"%s\","
       "\"tg_static_mem_bytes\":%d,\"pso_max_threads_per_tg\":%d,"
       "\"min_ms\":%.6f,\"median_ms\":%.6f,\"mean_ms\":%.6f,\"iters\":%d,"
-      "\"available_counter_sets\":[],\"profiling\":{\"counters_available\":false}}\n",
+      "\"available_counter_sets\":[],\"profiling\":{\"counters_available\":false,"
+      "\"enabled\":%s,\"profile_ms\":%.6f,\"nvtx_range\":\"mb_profile:%s\"}}\n",
       d.type, json_escape(d.name).c_str(), d.bucket, d.cpu_cores, d.sm_count,
       (unsigned long long)d.ram_bytes, json_escape(d.name).c_str(), json_escape(d.name).c_str(),
-      t.smem_bytes, t.threads_per_cta, t.min_ms, t.median_ms, t.mean_ms, t.iters);
+      t.smem_bytes, t.threads_per_cta, t.min_ms, t.median_ms, t.mean_ms, t.iters,
+      profile ? "true" : "false", t.profile_ms, json_escape(kernel.c_str()).c_str());
   mb_shutdown();
   return 0;
 }
