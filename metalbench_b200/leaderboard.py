@@ -74,18 +74,22 @@ def render_best_times(out: Path | None = None, session: Path | None = None) -> P
     reg, s = _registry(), _session(session)
     chips = _chips(s)
 
+    def entry(chip: str, name: str) -> dict:
+        return s.get(chip, {}).get(name) or {}
+
+    def num(v) -> bool:
+        return isinstance(v, (int, float)) and not isinstance(v, bool)
+
+    # "<best ms> (<speedup>×)" per chip, the cell format best_times.md readers
+    # parse; an entry without a positive speedup has no comparable time
     def cell(chip: str, name: str) -> str:
-        e = s.get(chip, {}).get(name)
-        if not e:
-            return "—"
-        ms, sp = e.get("best_time_ms"), e.get("speedup_vs_mlx")
-        if not isinstance(ms, (int, float)) or not isinstance(sp, (int, float)) or sp <= 0:
-            return "—"
-        return f"{ms:.3f} ({sp:.2f}×)"
+        e = entry(chip, name)
+        t, x = e.get("best_time_ms"), e.get("speedup_vs_mlx")
+        return f"{t:.3f} ({x:.2f}×)" if num(t) and num(x) and x > 0 else "—"
 
     def sol(chip: str, name: str) -> str:
-        v = s.get(chip, {}).get(name, {}).get("roofline_sol")
-        return f"{v * 100:.0f} %" if isinstance(v, (int, float)) else "—"
+        v = entry(chip, name).get("roofline_sol")
+        return f"{v * 100:.0f} %" if num(v) else "—"
 
     extra = [c for c in chips if c not in APPLE_CHIPS]
     head = ["kernel", "set"] + [c.replace("apple-", "").upper() for c in chips] + \
