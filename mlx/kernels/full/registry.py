@@ -18,11 +18,12 @@ _SCALARS = [dict(binding=6, dtype="u32", value=0), dict(binding=7, dtype="u32", 
 # Tolerance of the bf16 layer entries. rtol is the north-star bf16 bar (2e-2).
 # atol covers the absolute error floor of bf16 intermediates (normalised
 # activations, q/k/v, softmax weights, the SwiGLU activations summed over
-# K = 14336): measured, the errors have a standard deviation of about 8e-3
-# on outputs of rms ~1.4, so the all-elements verdict of the reference
-# (mlx/scripts/harness.py:26-33) over 33.5 M outputs needs atol = 6e-2
-# (7.5 sigma); 2e-2 failed 0.02-0.06 % of elements.
-BF16_LAYER_RTOL, BF16_LAYER_ATOL = 2e-2, 6e-2
+# K = 14336): measured, the errors have a standard deviation of 8-9e-3 on
+# outputs of rms ~1.4 with a heavy tail (the largest atol the reference's
+# all-elements verdict, mlx/scripts/harness.py:26-33, needed over six seeds
+# of the decode entry was 0.068, over the 33.5 M prefill outputs 0.046);
+# atol = 9e-2 is 10 sigma. 2e-2 failed 0.02-0.06 % of elements.
+BF16_LAYER_RTOL, BF16_LAYER_ATOL = 2e-2, 9e-2
 
 
 def _scalars(S):
