@@ -397,8 +397,8 @@ int choose_ksplit(int64_t M, int64_t N, int64_t K) {
 struct Plan {
   int64_t T;
   int ks_qkv, ks_o, ks_gu, ks_down;
-  size_t off_rstd1, off_rstd2, off_q, off_attn, off_x1, off_x1f, off_act, off_part, off_attn_ws,
-      total;
+  size_t off_rstd1, off_rstd2, off_q, off_attn, off_x1, off_x1f, off_p32, off_act, off_part,
+      off_attn_ws, total;
   size_t attn_ws;
 };
 
@@ -439,6 +439,7 @@ Plan make_plan(const Layer& L, int B, int S, int max_kv_len) {
   p.off_attn = o; o += a256(T * L.Dq * 2);
   p.off_x1 = o; o += a256(T * D * 2);
   p.off_x1f = o; o += a256(T * D * 4);
+  p.off_p32 = o; o += L.world > 1 ? a256(T * D * 4) : 0;  // this rank's fp32 partial product
   p.off_act = o; o += a256(T * L.FF * 2);
   p.off_part = o; o += a256(part);
   p.off_attn_ws = o; o += a256(p.attn_ws);
@@ -590,12 +591,16 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
   uint16_t* attn = reinterpret_cast<uint16_t*>(w + p.off_attn);
   uint16_t* x1 = reinterpret_cast<uint16_t*>(w + p.off_x1);
   float* x1f = reinterpret_cast<float*>(w + p.off_x1f);  // fp32 residual stream after attention
+  float* p32 = reinterpret_cast<float*>(w + p.off_p32);
   uint16_t* act = reinterpret_cast<uint16_t*>(w + p.off_act);
   float* part = reinterpret_cast<float*>(w + p.off_part);
   const int D = L.cfg.d_model, Dh = L.cfg.head_dim;
   const int64_t T = p.T;
   const int Nqkv = L.Dq + 2 * L.Dkv;
   const bool tp = L.world > 1;
+  // tensor parallel: fp32 partials summed over NVLink peer memory together
+  // with the residual step (else a bf16 NCCL all-reduce, then the residual)
+  const bool fused = tp && mb::tp_fused_ready((size_t)T, D);
   int rc;
 
   // 1. rstd1 (of the fp32 residual stream when the caller keeps one)
@@ -646,8 +651,10 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
 
   // The residual stream is added in fp32 and kept in fp32 (x1f); its bf16
   // copy x1 is the next GEMM's operand. One GPU: the o-proj epilogue adds
-  // it. Tensor parallel: the ranks' partial products (no residual) are
-  // all-reduced in bf16, then residual_add_kernel adds the fp32 residual.
+  // it. Tensor parallel: the ranks' fp32 partial products (no residual) are
+  // summed over NVLink peer memory by tp_reduce_residual, which also adds
+  // the residual (messages too large for its slots: bf16 NCCL all-reduce,
+  // then residual_add_kernel).
   bool rstd2_done = false;
   // 4. x1 = x + attn @ Wo
   EpiStore eo{};
@@ -661,6 +668,9 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
     eo.residual = x_res32 ? nullptr : x;
     eo.residual_f32 = x_res32;
     eo.out_f32_copy = x1f;
+  } else if (fused) {
+    eo.out = p32;
+    eo.out_f32 = 1;
   }
   if (p.ks_o > 1 || use_streamk(T, D)) {
     PartSum ps;
@@ -681,7 +691,11 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
     if (rc) return rc;
   }
   MB_CUDA(cudaGetLastError());
-  if (tp) {
+  if (fused) {
+    rc = mb::tp_reduce_residual(p32, T, D, x_res32, x, x1f, x1, rstd2, L.cfg.eps, s);
+    if (rc) return rc;
+    rstd2_done = true;
+  } else if (tp) {
     rc = mb::tp_allreduce_sum(x1, (size_t)T * D, s);
     if (rc) return rc;
     MB_CUDA(mb::launch_pdl(residual_add_kernel, dim3((unsigned)T), dim3(256), 0, s, x1, x_res32,
@@ -725,6 +739,9 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
   if (!tp) {
     ed.residual_f32 = x1f;
     ed.out_f32_copy = y_res32;
+  } else if (fused) {
+    ed.out = p32;
+    ed.out_f32 = 1;
   }
   if (p.ks_down > 1 || use_streamk(T, D)) {
     PartSum ps;
@@ -739,7 +756,10 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
     if (rc) return rc;
   }
   MB_CUDA(cudaGetLastError());
-  if (tp) {
+  if (fused) {
+    rc = mb::tp_reduce_residual(p32, T, D, x1f, nullptr, y_res32, y, nullptr, 0.f, s);
+    if (rc) return rc;
+  } else if (tp) {
     rc = mb::tp_allreduce_sum(y, (size_t)T * D, s);
     if (rc) return rc;
     MB_CUDA(mb::launch_pdl(residual_add_kernel, dim3((unsigned)T), dim3(256), 0, s, y,

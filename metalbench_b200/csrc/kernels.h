@@ -61,6 +61,13 @@ void tp_shutdown();
 int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream);
 int tp_world();
 int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
+// Fused fp32 peer reduction + residual (tp.cu): out = residual + sum over
+// ranks of part32 [T, D] (fp32, summed in rank order over NVLink), written as
+// fp32 (out32, optional) and bf16 (out16), with optional per-row rstd.
+bool tp_fused_ready(size_t T, int D);
+int tp_reduce_residual(const float* part32, int64_t T, int D, const float* res32,
+                       const uint16_t* res16, float* out32, uint16_t* out16, float* rstd_out,
+                       float eps, cudaStream_t stream);
 
 // gemm.cu: bf16 GEMM C[M, N] (row stride ldc) = act(A @ B) (+ residual, row
 // stride ld_res); b_layout 0: B [N, K], 1: B [K, N]; act 0 none, 1 exact GELU.

@@ -115,7 +115,7 @@ int tp_init(int rank, int world, const char* nccl_id_path, int timeout_ms) {
   int rc = wait_ready(timeout_ms, "NCCL communicator set-up");
   if (rc) return rc;
   g_world = world;
-  if (getenv("MB_TP_P2P") != nullptr) {  // peer all-reduce requested: map the peers
+  if (getenv("MB_TP_NCCL") == nullptr) {  // map the peers for the fused peer reduction
     rc = p2p_setup(rank, world);
     if (rc) return rc;
   }
@@ -183,7 +183,8 @@ int tp_allreduce_bf16(void* buf, size_t count, cudaStream_t stream) {
 // ---------------------------------------------------------------------------
 static constexpr size_t kP2PMaxElems = size_t(4) << 20;  // 8 MiB of bf16 per slot
 static constexpr size_t kP2PRegion =
-    4 * kP2PMaxElems * sizeof(uint16_t) + 2 * 64 * sizeof(uint32_t);
+    4 * kP2PMaxElems * sizeof(uint16_t) + 2 * 64 * sizeof(uint32_t) + 256 +
+    2 * kP2PMaxElems * sizeof(float);
 
 struct Region {  // offsets inside one rank's region
   static __host__ __device__ uint16_t* staging(void* base, uint32_t slot) {
@@ -196,6 +197,12 @@ struct Region {  // offsets inside one rank's region
     return reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(base) + 4 * kP2PMaxElems);
   }
   static __host__ __device__ uint32_t* flags2(void* base) { return flags(base) + 64; }
+  // fp32 partials of the fused reduce + residual step, [2][kP2PMaxElems]
+  static __host__ __device__ float* staging32(void* base, uint32_t slot) {
+    uint8_t* p = reinterpret_cast<uint8_t*>(flags2(base) + 64);
+    p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
+    return reinterpret_cast<float*>(p) + (size_t)slot * kP2PMaxElems;
+  }
 };
 
 struct P2P {
@@ -325,6 +332,86 @@ __global__ void p2p_collect_kernel(uint16_t* __restrict__ out, size_t n, PeerPtr
     reinterpret_cast<uint4*>(out)[i] = res[i];
 }
 
+// Fused tensor-parallel reduce + residual (the decoder's o-proj and down-proj
+// step). Each rank publishes its fp32 partial product [T, D] into its
+// staging32 slot (double-buffered by epoch, flags as above), then one CTA per
+// row waits for every rank, sums the W partials in fp32 over NVLink in rank
+// order (so every rank computes bitwise the same value), adds the fp32 (or
+// bf16) residual and writes the fp32 stream, its bf16 copy and optionally
+// rstd = rsqrt(mean(out^2) + eps). Nothing is rounded to bf16 before the sum.
+__global__ void p2p_publish_f32_kernel(const float* __restrict__ src, size_t n, PeerPtrs peers,
+                                       uint32_t* ctr, int rank, int world) {
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]);
+  float* dst = Region::staging32(peers.r[rank], e & 1);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 4;
+       i += (size_t)gridDim.x * blockDim.x)
+    reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(&ctr[1], 1u) + 1 == gridDim.x) {  // the last CTA of this rank
+      __threadfence_system();
+      for (int r = 0; r < world; ++r) store_release_sys(Region::flags(peers.r[r]) + rank, e + 1);
+      ctr[1] = 0;
+      ctr[0] = e + 1;
+    }
+  }
+}
+
+__global__ void p2p_reduce_residual_kernel(PeerPtrs peers, const uint32_t* ctr, int rank,
+                                           int world, int D, const float* __restrict__ res32,
+                                           const uint16_t* __restrict__ res16,
+                                           float* __restrict__ out32, uint16_t* __restrict__ out16,
+                                           float* __restrict__ rstd_out, float eps,
+                                           uint32_t* status) {
+  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(&ctr[0]);  // already bumped
+  wait_flags(Region::flags(peers.r[rank]), e, world, status);
+  const uint32_t slot = (e - 1) & 1;
+  const int64_t row = blockIdx.x;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 4; c < D; c += blockDim.x * 4) {
+    const int64_t off = row * D + c;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < world; ++r) {
+      const float4 t = *reinterpret_cast<const float4*>(Region::staging32(peers.r[r], slot) + off);
+      a.x += t.x;
+      a.y += t.y;
+      a.z += t.z;
+      a.w += t.w;
+    }
+    if (res32) {
+      const float4 t = *reinterpret_cast<const float4*>(res32 + off);
+      a.x += t.x;
+      a.y += t.y;
+      a.z += t.z;
+      a.w += t.w;
+    } else {
+      const uint2 t = *reinterpret_cast<const uint2*>(res16 + off);
+      a.x += __uint_as_float(t.x << 16);
+      a.y += __uint_as_float(t.x & 0xFFFF0000u);
+      a.z += __uint_as_float(t.y << 16);
+      a.w += __uint_as_float(t.y & 0xFFFF0000u);
+    }
+    if (out32) *reinterpret_cast<float4*>(out32 + off) = a;
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w);
+    *reinterpret_cast<uint2*>(out16 + off) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+    ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+  }
+  if (!rstd_out) return;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float wsum[32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) wsum[w] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) t += wsum[i];
+    rstd_out[row] = rsqrtf(t / (float)D + eps);
+  }
+}
+
 #ifdef MB_HAVE_NCCL
 static int p2p_setup(int rank, int world) {
   if (world > 8) {
@@ -379,10 +466,9 @@ static void p2p_teardown() {
   p = P2P();
 }
 
-// All-reduce used by the decoder. NCCL by default: on 8 B200s with NVLS it
-// measured faster than both peer variants at the decode message size (1 MiB:
-// stack decode 30958 tok/s with NCCL, 28442 one-shot, 24894 two-shot).
-// MB_TP_P2P=1shot|2shot selects the peer kernels for messages that fit a slot.
+// bf16 all-reduce (used when the fused fp32 peer reduction does not apply,
+// e.g. prefill messages larger than a slot). NCCL by default; MB_TP_P2P=
+// 1shot|2shot selects the bf16 peer kernels for messages that fit a slot.
 int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream) {
   static const char* mode = getenv("MB_TP_P2P");
   static const bool use_p2p = mode && (!strcmp(mode, "1shot") || !strcmp(mode, "2shot"));
@@ -412,6 +498,34 @@ int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream) {
     p2p_collect_kernel<<<grid(count / 8), 256, 0, stream>>>(x, count, pp, g_p2p.ctr, R, W,
                                                             device_status_ptr());
   }
+  MB_CUDA(cudaGetLastError());
+  return MB_OK;
+}
+
+bool tp_fused_ready(size_t T, int D) {
+  static const bool off = getenv("MB_TP_NCCL") != nullptr;
+  return g_p2p.ready && !off && (size_t)T * D <= kP2PMaxElems && D % 4 == 0;
+}
+
+int tp_reduce_residual(const float* part32, int64_t T, int D, const float* res32,
+                       const uint16_t* res16, float* out32, uint16_t* out16, float* rstd_out,
+                       float eps, cudaStream_t stream) {
+  MB_REQUIRE(tp_fused_ready((size_t)T, D), "fused TP reduce: peers not mapped or size too large");
+  MB_REQUIRE(res32 || res16, "fused TP reduce: no residual");
+  PeerPtrs pp;
+  for (int q = 0; q < 8; ++q) pp.r[q] = g_p2p.peer[q];
+  const size_t n = (size_t)T * D;
+  int pub = (int)((n / 4 + 255) / 256);
+  if (pub > 2 * num_sms()) pub = 2 * num_sms();
+  if (pub < 1) pub = 1;
+  p2p_publish_f32_kernel<<<pub, 256, 0, stream>>>(part32, n, pp, g_p2p.ctr, g_p2p.rank,
+                                                  g_p2p.world);
+  MB_CUDA(cudaGetLastError());
+  int threads = D / 4 < 1024 ? ((D / 4 + 31) / 32) * 32 : 1024;
+  if (threads < 32) threads = 32;
+  p2p_reduce_residual_kernel<<<(unsigned)T, threads, 0, stream>>>(
+      pp, g_p2p.ctr, g_p2p.rank, g_p2p.world, D, res32, res16, out32, out16, rstd_out, eps,
+      device_status_ptr());
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
