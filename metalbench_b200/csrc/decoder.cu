@@ -601,6 +601,7 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
   // tensor parallel: fp32 partials summed over NVLink peer memory together
   // with the residual step (else a bf16 NCCL all-reduce, then the residual)
   const bool fused = tp && mb::tp_fused_ready((size_t)T, D);
+  if (fused) p32 = mb::tp_partial_slot();  // the partial goes straight to peer-mapped memory
   int rc;
 
   // 1. rstd1 (of the fp32 residual stream when the caller keeps one)

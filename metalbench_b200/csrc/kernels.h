@@ -64,7 +64,10 @@ int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 // Fused fp32 peer reduction + residual (tp.cu): out = residual + sum over
 // ranks of part32 [T, D] (fp32, summed in rank order over NVLink), written as
 // fp32 (out32, optional) and bf16 (out16), with optional per-row rstd.
+// tp_partial_slot() is this rank's peer-mapped partial buffer: a producer that
+// writes its partial there directly saves the copy in tp_reduce_residual.
 bool tp_fused_ready(size_t T, int D);
+float* tp_partial_slot();
 int tp_reduce_residual(const float* part32, int64_t T, int D, const float* res32,
                        const uint16_t* res16, float* out32, uint16_t* out16, float* rstd_out,
                        float eps, cudaStream_t stream);

@@ -221,6 +221,9 @@ struct PeerPtrs {
 __device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void store_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -333,82 +336,131 @@ __global__ void p2p_collect_kernel(uint16_t* __restrict__ out, size_t n, PeerPtr
 }
 
 // Fused tensor-parallel reduce + residual (the decoder's o-proj and down-proj
-// step). Each rank publishes its fp32 partial product [T, D] into its
-// staging32 slot (double-buffered by epoch, flags as above), then one CTA per
-// row waits for every rank, sums the W partials in fp32 over NVLink in rank
-// order (so every rank computes bitwise the same value), adds the fp32 (or
-// bf16) residual and writes the fp32 stream, its bf16 copy and optionally
-// rstd = rsqrt(mean(out^2) + eps). Nothing is rounded to bf16 before the sum.
-__global__ void p2p_publish_f32_kernel(const float* __restrict__ src, size_t n, PeerPtrs peers,
-                                       uint32_t* ctr, int rank, int world) {
-  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]);
-  float* dst = Region::staging32(peers.r[rank], e & 1);
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 4;
-       i += (size_t)gridDim.x * blockDim.x)
-    reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+// step), two phases over NVLink peer memory. Each rank's fp32 partial product
+// [T, D] sits in its staging32 slot 0 (the decoder's epilogue writes it there
+// directly). Rows are owned in contiguous blocks of ceil(T / W).
+//   reduce   : CTA 0 signals flags[my rank] = e on every peer, every CTA
+//              waits for all flags >= e, then sums the W partials of MY rows
+//              in rank order (0..W-1, fp32), adds the fp32 (or bf16) residual
+//              and stores the row into my staging32 slot 1 (the result area).
+//              The last CTA signals flags2[my rank] = e on every peer.
+//   gather   : one CTA per row waits for flags2[owner] >= e, reads the
+//              owner's result row (local for my own rows), writes the fp32
+//              stream, its bf16 copy and optionally rstd = rsqrt(mean(out^2) +
+//              eps). The last CTA bumps the epoch.
+// NVLink bytes per rank: (W-1)/W of the partial in, (W-1)/W of the result in,
+// against (W-1) whole partials for a one-shot sum. Each row is summed by one
+// rank and copied by the others, so every rank holds bitwise the same stream.
+// One slot of each kind suffices: a rank rewrites its partial (next call)
+// only after its gather saw every owner's flags2, i.e. after every peer read
+// it; it rewrites its result rows only after every peer signalled the next
+// call's reduce, i.e. after every peer's gather finished.
+__global__ void p2p_rs_kernel(PeerPtrs peers, uint32_t* ctr, int rank, int world, int64_t T, int D,
+                              const float* __restrict__ res32, const uint16_t* __restrict__ res16,
+                              uint32_t* status) {
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]) + 1;
+  // The partial was written by an earlier kernel on this stream, so it is
+  // complete in this GPU's memory (which serves the peers' reads) before this
+  // grid starts: a relaxed store is enough to announce it. One CTA signals
+  // (the grid is at most one CTA per SM, so all CTAs are resident at once).
+  if (blockIdx.x == 0 && threadIdx.x < (unsigned)world)
+    store_relaxed_sys(Region::flags(peers.r[threadIdx.x]) + rank, e);
+  wait_flags(Region::flags(peers.r[rank]), e, world, status);
+  const int64_t per = (T + world - 1) / world;
+  const int64_t r0 = (int64_t)rank * per;
+  const int64_t r1 = r0 + per < T ? r0 + per : T;
+  const int64_t base = r0 * D / 4, n4 = r1 > r0 ? (r1 - r0) * D / 4 : 0;
+  float4* out = reinterpret_cast<float4*>(Region::staging32(peers.r[rank], 1));
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = base + i;
+    float4 t[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < world) t[r] = reinterpret_cast<const float4*>(Region::staging32(peers.r[r], 0))[j];
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < world) {
+        a.x += t[r].x;
+        a.y += t[r].y;
+        a.z += t[r].z;
+        a.w += t[r].w;
+      }
+    if (res32) {
+      const float4 u = reinterpret_cast<const float4*>(res32)[j];
+      a.x += u.x;
+      a.y += u.y;
+      a.z += u.z;
+      a.w += u.w;
+    } else {
+      const uint2 u = reinterpret_cast<const uint2*>(res16)[j];
+      a.x += __uint_as_float(u.x << 16);
+      a.y += __uint_as_float(u.x & 0xFFFF0000u);
+      a.z += __uint_as_float(u.y << 16);
+      a.w += __uint_as_float(u.y & 0xFFFF0000u);
+    }
+    out[j] = a;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    // GPU-scope fence per CTA; the last CTA's system-scope release is
+    // cumulative over the writes it observed through the arrival counter.
+    __threadfence();
     if (atomicAdd(&ctr[1], 1u) + 1 == gridDim.x) {  // the last CTA of this rank
       __threadfence_system();
-      for (int r = 0; r < world; ++r) store_release_sys(Region::flags(peers.r[r]) + rank, e + 1);
+      for (int r = 0; r < world; ++r) store_release_sys(Region::flags2(peers.r[r]) + rank, e);
       ctr[1] = 0;
-      ctr[0] = e + 1;
     }
   }
 }
 
-__global__ void p2p_reduce_residual_kernel(PeerPtrs peers, const uint32_t* ctr, int rank,
-                                           int world, int D, const float* __restrict__ res32,
-                                           const uint16_t* __restrict__ res16,
-                                           float* __restrict__ out32, uint16_t* __restrict__ out16,
-                                           float* __restrict__ rstd_out, float eps,
-                                           uint32_t* status) {
-  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(&ctr[0]);  // already bumped
-  wait_flags(Region::flags(peers.r[rank]), e, world, status);
-  const uint32_t slot = (e - 1) & 1;
+__global__ void p2p_ag_kernel(PeerPtrs peers, uint32_t* ctr, int rank, int world, int64_t T, int D,
+                              float* __restrict__ out32, uint16_t* __restrict__ out16,
+                              float* __restrict__ rstd_out, float eps, uint32_t* status) {
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]) + 1;
   const int64_t row = blockIdx.x;
+  const int64_t per = (T + world - 1) / world;
+  const int owner = (int)(row / per);
+  if (threadIdx.x == 0) {
+    const uint32_t* f = Region::flags2(peers.r[rank]) + owner;
+    const uint64_t t0 = mbd::globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      if ((int32_t)(load_acquire_sys(f) - e) >= 0) break;
+      if ((it & 63u) == 0 && mbd::globaltimer_ns() - t0 > 5000000000ull) {
+        atomicOr(status, MB_DEV_TIMEOUT_EPI);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const float* src = Region::staging32(peers.r[owner], 1);
   float ss = 0.f;
   for (int c = threadIdx.x * 4; c < D; c += blockDim.x * 4) {
     const int64_t off = row * D + c;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = 0; r < world; ++r) {
-      const float4 t = *reinterpret_cast<const float4*>(Region::staging32(peers.r[r], slot) + off);
-      a.x += t.x;
-      a.y += t.y;
-      a.z += t.z;
-      a.w += t.w;
-    }
-    if (res32) {
-      const float4 t = *reinterpret_cast<const float4*>(res32 + off);
-      a.x += t.x;
-      a.y += t.y;
-      a.z += t.z;
-      a.w += t.w;
-    } else {
-      const uint2 t = *reinterpret_cast<const uint2*>(res16 + off);
-      a.x += __uint_as_float(t.x << 16);
-      a.y += __uint_as_float(t.x & 0xFFFF0000u);
-      a.z += __uint_as_float(t.y << 16);
-      a.w += __uint_as_float(t.y & 0xFFFF0000u);
-    }
+    const float4 a = *reinterpret_cast<const float4*>(src + off);
     if (out32) *reinterpret_cast<float4*>(out32 + off) = a;
     __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w);
     *reinterpret_cast<uint2*>(out16 + off) =
         make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
     ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
   }
-  if (!rstd_out) return;
+  if (rstd_out) {
 #pragma unroll
-  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  __shared__ float wsum[32];
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) wsum[w] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) t += wsum[i];
-    rstd_out[row] = rsqrtf(t / (float)D + eps);
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    __shared__ float wsum[32];
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) wsum[w] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) t += wsum[i];
+      rstd_out[row] = rsqrtf(t / (float)D + eps);
+    }
+  }
+  if (threadIdx.x == 0 && atomicAdd(&ctr[2], 1u) + 1 == gridDim.x) {  // the last CTA
+    ctr[2] = 0;
+    ctr[0] = e;
   }
 }
 
@@ -507,25 +559,34 @@ bool tp_fused_ready(size_t T, int D) {
   return g_p2p.ready && !off && (size_t)T * D <= kP2PMaxElems && D % 4 == 0;
 }
 
+float* tp_partial_slot() {
+  return g_p2p.ready ? Region::staging32(g_p2p.region, 0) : nullptr;
+}
+
 int tp_reduce_residual(const float* part32, int64_t T, int D, const float* res32,
                        const uint16_t* res16, float* out32, uint16_t* out16, float* rstd_out,
                        float eps, cudaStream_t stream) {
   MB_REQUIRE(tp_fused_ready((size_t)T, D), "fused TP reduce: peers not mapped or size too large");
   MB_REQUIRE(res32 || res16, "fused TP reduce: no residual");
+  MB_REQUIRE(T > 0, "fused TP reduce: no rows");
   PeerPtrs pp;
   for (int q = 0; q < 8; ++q) pp.r[q] = g_p2p.peer[q];
   const size_t n = (size_t)T * D;
-  int pub = (int)((n / 4 + 255) / 256);
-  if (pub > 2 * num_sms()) pub = 2 * num_sms();
-  if (pub < 1) pub = 1;
-  p2p_publish_f32_kernel<<<pub, 256, 0, stream>>>(part32, n, pp, g_p2p.ctr, g_p2p.rank,
-                                                  g_p2p.world);
+  float* slot = tp_partial_slot();
+  if (part32 != slot)
+    MB_CUDA(cudaMemcpyAsync(slot, part32, n * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+  const int W = g_p2p.world;
+  const int64_t per = (T + W - 1) / W;
+  int rs = (int)((per * D / 4 + 255) / 256);
+  if (rs > num_sms()) rs = num_sms();
+  if (rs < 1) rs = 1;
+  p2p_rs_kernel<<<rs, 256, 0, stream>>>(pp, g_p2p.ctr, g_p2p.rank, W, T, D, res32, res16,
+                                        device_status_ptr());
   MB_CUDA(cudaGetLastError());
   int threads = D / 4 < 1024 ? ((D / 4 + 31) / 32) * 32 : 1024;
   if (threads < 32) threads = 32;
-  p2p_reduce_residual_kernel<<<(unsigned)T, threads, 0, stream>>>(
-      pp, g_p2p.ctr, g_p2p.rank, g_p2p.world, D, res32, res16, out32, out16, rstd_out, eps,
-      device_status_ptr());
+  p2p_ag_kernel<<<(unsigned)T, threads, 0, stream>>>(pp, g_p2p.ctr, g_p2p.rank, W, T, D, out32,
+                                                     out16, rstd_out, eps, device_status_ptr());
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
