@@ -307,6 +307,21 @@ struct DecodeProducer {
     mbd::prefetch_tmap(&b);
   }
   __device__ void load_resident(uint8_t*, uint64_t*) const {}
+  // B is the layer's packed weight, which no kernel of the stream writes: the
+  // kernel requests the B boxes of its first ring stages before it waits for
+  // the previous kernel (programmatic dependent launch), so the weight stream
+  // overlaps that kernel's tail; A, the activations, follows after the wait.
+  static constexpr bool PRELOAD_B = true;
+  __device__ void load_a(uint8_t* st, uint64_t* bar, int tm, int, int kb) const {
+    mbd::tma_load_2d(st, &a, bar, kb * KE, tm * BM);
+  }
+  __device__ void load_b(uint8_t* st, uint64_t* bar, int, int tn, int kb) const {
+    if (b_tiled)
+      mbd::bulk_load(st + AROWS * KBYTES, b_tiled + ((size_t)tn * b_kblocks + kb) * (BN * KBYTES),
+                     BN * KBYTES, bar);
+    else
+      mbd::tma_load_2d(st + AROWS * KBYTES, &b, bar, kb * KE, tn * BN);
+  }
   __device__ void load(uint8_t* st, uint64_t* bar, int tm, int tn, int kb) const {
     mbd::tma_load_2d(st, &a, bar, kb * KE, tm * BM);
     if (b_tiled)
@@ -324,6 +339,12 @@ struct DecodeProducer {
                    (!first || kk > 0) ? 1u : 0u);
   }
 };
+
+// preload_b<P>::value: P::PRELOAD_B when the producer declares it.
+template <class P, class = void>
+struct preload_b : std::false_type {};
+template <class P>
+struct preload_b<P, std::void_t<decltype(P::PRELOAD_B)>> : std::bool_constant<P::PRELOAD_B> {};
 
 // PROMOTE > 0: the accumulation is cut into chunks of PROMOTE k-blocks. Each
 // chunk is summed by the tensor core into a fresh TMEM accumulator and the
@@ -399,6 +420,20 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t tmem = *tmem_slot;
   // set-up above overlaps the previous kernel when launched with PDL
   mbd::pdl_trigger();
+  int npre = 0;  // leading ring stages whose B box was requested before the wait
+  if constexpr (preload_b<Producer>::value) {
+    if (warp == 0) {
+      if (lane == 0) {
+        int tm, tn, ks, kb0, kb1;
+        for (int u = 0; npre < STAGES && unit(u, tm, tn, ks, kb0, kb1); ++u)
+          for (int kb = kb0; kb < kb1 && npre < STAGES; ++kb, ++npre) {
+            mbd::mbar_expect_tx(&full[npre], prod.stage_tx_bytes());
+            prod.load_b(sA(npre), &full[npre], tm, tn, kb);
+          }
+      }
+      npre = __shfl_sync(0xffffffffu, npre, 0);
+    }
+  }
   mbd::pdl_wait();
 
   // The producer and MMA warps run their loops with all 32 lanes (waits on
@@ -420,17 +455,24 @@ __global__ void __launch_bounds__(256, 1)
       __syncwarp();
     }
     int tm, tn, ks, kb0, kb1;
+    int cnt = 0;
     for (int u = 0; ok && unit(u, tm, tn, ks, kb0, kb1); ++u) {
-      for (int kb = kb0; kb < kb1; ++kb) {
-        const bool got =
-            mbd::mbar_wait(&empty[stage], phase ^ 1, status, MB_DEV_TIMEOUT_TMA, abort_flag);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          mbd::mbar_expect_tx(&full[stage], prod.stage_tx_bytes());
-          prod.load(sA(stage), &full[stage], tm, tn, kb);
+      for (int kb = kb0; kb < kb1; ++kb, ++cnt) {
+        if (cnt < npre) {  // first use of this stage; its B box is on the way
+          if constexpr (preload_b<Producer>::value) {
+            if (lane == 0) prod.load_a(sA(stage), &full[stage], tm, tn, kb);
+          }
+        } else {
+          const bool got =
+              mbd::mbar_wait(&empty[stage], phase ^ 1, status, MB_DEV_TIMEOUT_TMA, abort_flag);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            mbd::mbar_expect_tx(&full[stage], prod.stage_tx_bytes());
+            prod.load(sA(stage), &full[stage], tm, tn, kb);
+          }
         }
         __syncwarp();
         issued = (issued & ~(1u << stage)) | (phase << stage);

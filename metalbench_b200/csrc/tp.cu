@@ -358,6 +358,11 @@ __global__ void p2p_collect_kernel(uint16_t* __restrict__ out, size_t n, PeerPtr
 __global__ void p2p_rs_kernel(PeerPtrs peers, uint32_t* ctr, int rank, int world, int64_t T, int D,
                               const float* __restrict__ res32, const uint16_t* __restrict__ res16,
                               uint32_t* status) {
+  // Launched with programmatic dependent launch: let the next kernels start
+  // their set-up (the next GEMM also requests its first weight boxes), then
+  // wait for the kernel that wrote the partial before touching anything.
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]) + 1;
   // The partial was written by an earlier kernel on this stream, so it is
   // complete in this GPU's memory (which serves the peers' reads) before this
@@ -418,6 +423,8 @@ __global__ void p2p_rs_kernel(PeerPtrs peers, uint32_t* ctr, int rank, int world
 __global__ void p2p_ag_kernel(PeerPtrs peers, uint32_t* ctr, int rank, int world, int64_t T, int D,
                               float* __restrict__ out32, uint16_t* __restrict__ out16,
                               float* __restrict__ rstd_out, float eps, uint32_t* status) {
+  mbd::pdl_trigger();
+  mbd::pdl_wait();
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]) + 1;
   const int64_t row = blockIdx.x;
   const int64_t per = (T + world - 1) / world;
@@ -580,13 +587,13 @@ int tp_reduce_residual(const float* part32, int64_t T, int D, const float* res32
   int rs = (int)((per * D / 4 + 255) / 256);
   if (rs > num_sms()) rs = num_sms();
   if (rs < 1) rs = 1;
-  p2p_rs_kernel<<<rs, 256, 0, stream>>>(pp, g_p2p.ctr, g_p2p.rank, W, T, D, res32, res16,
-                                        device_status_ptr());
+  MB_CUDA(launch_pdl(p2p_rs_kernel, dim3(rs), dim3(256), 0, stream, pp, g_p2p.ctr, g_p2p.rank, W,
+                     T, D, res32, res16, device_status_ptr()));
   MB_CUDA(cudaGetLastError());
   int threads = D / 4 < 1024 ? ((D / 4 + 31) / 32) * 32 : 1024;
   if (threads < 32) threads = 32;
-  p2p_ag_kernel<<<(unsigned)T, threads, 0, stream>>>(pp, g_p2p.ctr, g_p2p.rank, W, T, D, out32,
-                                                     out16, rstd_out, eps, device_status_ptr());
+  MB_CUDA(launch_pdl(p2p_ag_kernel, dim3((unsigned)T), dim3(threads), 0, stream, pp, g_p2p.ctr,
+                     g_p2p.rank, W, T, D, out32, out16, rstd_out, eps, device_status_ptr()));
   MB_CUDA(cudaGetLastError());
   return MB_OK;
 }
