@@ -154,16 +154,37 @@ __device__ __forceinline__ void sum_slots(const float* __restrict__ part, const 
 #pragma unroll
   for (int j = 0; j < RW; ++j) v[j] = 0.f;
   const int n = ps.count(col);
-  for (int k0 = 0; k0 < n; k0 += 4) {
-    float4 t[4][RW / 4];  // up to four slots' loads in flight before any add
+  const float* p0 = part + (int64_t)row * N + col;
+  // Whole batches of eight slots: all sixteen 16-byte loads are issued before
+  // any add (stream-K at tensor-parallel sizes leaves ~30 slots per column of
+  // a narrow GEMM, and these kernels run few threads). The adds stay in slot
+  // order 0..n-1 in every case.
+  int k0 = 0;
+  for (; k0 + 8 <= n; k0 += 8) {
+    float4 t[8][RW / 4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4* p =
-          reinterpret_cast<const float4*>(part + (k0 + k) * ps.stride + (int64_t)row * N + col);
+    for (int k = 0; k < 8; ++k)
 #pragma unroll
       for (int j = 0; j < RW / 4; ++j)
-        t[k][j] = k0 + k < n ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+        t[k][j] = __ldcg(reinterpret_cast<const float4*>(p0 + (k0 + k) * ps.stride) + j);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+      for (int j = 0; j < RW / 4; ++j) {
+        v[4 * j] += t[k][j].x;
+        v[4 * j + 1] += t[k][j].y;
+        v[4 * j + 2] += t[k][j].z;
+        v[4 * j + 3] += t[k][j].w;
+      }
+  }
+  for (; k0 < n; k0 += 4) {
+    float4 t[4][RW / 4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < RW / 4; ++j)
+        t[k][j] = k0 + k < n ? __ldcg(reinterpret_cast<const float4*>(p0 + (k0 + k) * ps.stride) + j)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
