@@ -64,6 +64,8 @@ int tp_allreduce_sum(void* buf, size_t count, cudaStream_t stream);
 // Fused fp32 peer reduction + residual (tp.cu): out = residual + sum over
 // ranks of part32 [T, D] (fp32, summed in rank order over NVLink), written as
 // fp32 (out32, optional) and bf16 (out16), with optional per-row rstd.
+// One set of peer slots per process: calls must be serialised on the GPU (one
+// stream) and issued in the same order on every rank.
 // tp_partial_slot() is this rank's peer-mapped partial buffer: a producer that
 // writes its partial there directly saves the copy in tp_reduce_residual.
 bool tp_fused_ready(size_t T, int D);
