@@ -366,8 +366,9 @@ __global__ void p2p_rs_kernel(PeerPtrs peers, uint32_t* ctr, int rank, int world
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&ctr[0]) + 1;
   // The partial was written by an earlier kernel on this stream, so it is
   // complete in this GPU's memory (which serves the peers' reads) before this
-  // grid starts: a relaxed store is enough to announce it. One CTA signals
-  // (the grid is at most one CTA per SM, so all CTAs are resident at once).
+  // grid starts: a relaxed store is enough to announce it. CTA 0 signals for
+  // the grid; nothing that runs before it on this GPU waits on this grid, so
+  // it always gets an SM even if its siblings are spinning already.
   if (blockIdx.x == 0 && threadIdx.x < (unsigned)world)
     store_relaxed_sys(Region::flags(peers.r[threadIdx.x]) + rank, e);
   wait_flags(Region::flags(peers.r[rank]), e, world, status);
