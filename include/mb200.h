@@ -256,8 +256,10 @@ int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, 
  * input's residual (x must hold its bf16 rounding; null = use x), and when
  * y_res32 is not null it receives the fp32 output beside the bf16 y. Inside
  * the layer the residual adds are fp32 in either case; under tensor
- * parallelism the ranks' partial products are all-reduced in bf16 and the
- * residual is added after the reduction. Same reference as
+ * parallelism the ranks' fp32 partial products are summed in rank order over
+ * NVLink peer memory together with the residual (messages above the peer
+ * slot, i.e. prefill: a bf16 NCCL all-reduce, then the residual add). Same
+ * reference as
  * mb_decoder_layer_forward (mlx/kernels/full/llama_decoder_layer.py:24-46,
  * whose x stays fp32 throughout). */
 int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x, const float* x_res32,
@@ -265,6 +267,21 @@ int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x, const floa
                                 const int* kv_len, int max_kv_len, uint16_t* k_cache,
                                 uint16_t* v_cache, const int* block_table, int max_pages,
                                 int causal, void* workspace, size_t workspace_bytes, void* stream);
+
+/* mb_decoder_layer_forward_ex for layers chained in a stack: the input-side
+ * RMSNorm factor of layer l+1, rstd = rsqrt(mean(y_res32^2) + eps) per row, is
+ * written by layer l into rstd_out [B*S] fp32 (needs y_res32) from the kernel
+ * that forms each output row, and layer l+1 takes it as rstd_in instead of
+ * computing it again (null = compute it). Both layers must share eps. Same
+ * reference as mb_decoder_layer_forward (the `_rms_norm` of the next layer's
+ * input, mlx/kernels/full/llama_decoder_layer.py:48-50). */
+int mb_decoder_layer_forward_chain(const void* layer, const uint16_t* x, const float* x_res32,
+                                   const float* rstd_in, uint16_t* y, float* y_res32,
+                                   float* rstd_out, int B, int S, const int* start_pos,
+                                   const int* kv_len, int max_kv_len, uint16_t* k_cache,
+                                   uint16_t* v_cache, const int* block_table, int max_pages,
+                                   int causal, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 /* fp32 decoder layer for the reference's own llama_decoder_layer_f32 entry
  * (mlx/kernels/full/llama_decoder_layer.py:24-64; registry

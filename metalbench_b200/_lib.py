@@ -104,6 +104,8 @@ SIGNATURES = {
                                            C.c_size_t, _P]),
     "mb_decoder_layer_forward_ex": (C.c_int, [_P, _P, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P,
                                               _I, _I, _P, C.c_size_t, _P]),
+    "mb_decoder_layer_forward_chain": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _I,
+                                                 _P, _P, _P, _I, _I, _P, C.c_size_t, _P]),
     "mb_tp_allreduce_bf16": (C.c_int, [_P, C.c_size_t, _P]),
     "mb_rms_norm_linear_workspace_bytes": (C.c_size_t, [_I64]),
     "mb_rms_norm_linear_bf16": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, C.c_float, _P,

@@ -584,15 +584,15 @@ extern "C" size_t mb_decoder_layer_workspace_bytes(const void* layer, int B, int
   return make_plan(*static_cast<const Layer*>(layer), B, S, max_kv_len).total;
 }
 
-extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
-                                           const float* x_res32, uint16_t* y, float* y_res32,
-                                           int B, int S, const int* start_pos, const int* kv_len,
-                                           int max_kv_len, uint16_t* k_cache, uint16_t* v_cache,
-                                           const int* block_table, int max_pages, int causal,
-                                           void* workspace, size_t workspace_bytes,
-                                           void* stream) {
+namespace {
+int decoder_forward(const void* layer, const uint16_t* x, const float* x_res32, uint16_t* y,
+                    float* y_res32, const float* rstd_in, float* rstd_out, int B, int S,
+                    const int* start_pos, const int* kv_len, int max_kv_len, uint16_t* k_cache,
+                    uint16_t* v_cache, const int* block_table, int max_pages, int causal,
+                    void* workspace, size_t workspace_bytes, void* stream) {
   MB_REQUIRE(layer && x && y && start_pos && kv_len && k_cache && v_cache && block_table,
              "decoder forward: null argument");
+  MB_REQUIRE(!rstd_out || y_res32, "decoder forward: rstd_out needs the fp32 output y_res32");
   MB_REQUIRE(B >= 0 && S >= 0, "decoder forward: negative size");
   if (B == 0 || S == 0) return MB_OK;
   const Layer& L = *static_cast<const Layer*>(layer);
@@ -625,8 +625,11 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
   if (fused) p32 = mb::tp_partial_slot();  // the partial goes straight to peer-mapped memory
   int rc;
 
-  // 1. rstd1 (of the fp32 residual stream when the caller keeps one)
-  if (x_res32)
+  // 1. rstd1 (of the fp32 residual stream when the caller keeps one), unless
+  // the previous layer of a stack already produced it
+  if (rstd_in)
+    rstd1 = const_cast<float*>(rstd_in);
+  else if (x_res32)
     MB_CUDA(mb::launch_pdl(rownorm_f32_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
                             x_res32, (int)T, D, L.cfg.eps, rstd1));
   else
@@ -769,6 +772,8 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
     PartSum ps;
     rc = gemm_partial(act, L.wdown, part, T, D, L.FF, p.ks_down, s, &ps);
     if (rc) return rc;
+    // (one CTA per row could also yield the next rstd1, but at T = 64 that
+    // leaves most SMs idle in a latency-bound reduce: rownorm follows instead)
     MB_CUDA(mb::launch_pdl(reduce_store_kernel, dim3(blocks_for(T * D / RW)), dim3(256), 0, s,
                             part, ps, (int)T, D, ed, (float*)nullptr, 0.f));
   } else {
@@ -778,17 +783,50 @@ extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
     if (rc) return rc;
   }
   MB_CUDA(cudaGetLastError());
+  // rstd_out: the next layer's rstd1, rsqrt(mean(y_res32^2) + eps), from the
+  // kernel that forms the output row under tensor parallelism (the peer
+  // reduce, the residual add); on one GPU by rownorm_f32_kernel, the same
+  // launch on the same input that the next layer would otherwise make
   if (fused) {
-    rc = mb::tp_reduce_residual(p32, T, D, x1f, nullptr, y_res32, y, nullptr, 0.f, s);
+    rc = mb::tp_reduce_residual(p32, T, D, x1f, nullptr, y_res32, y, rstd_out, L.cfg.eps, s);
     if (rc) return rc;
   } else if (tp) {
     rc = mb::tp_allreduce_sum(y, (size_t)T * D, s);
     if (rc) return rc;
     MB_CUDA(mb::launch_pdl(residual_add_kernel, dim3((unsigned)T), dim3(256), 0, s, y,
-                            (const float*)x1f, (const uint16_t*)nullptr, y_res32, D,
-                            (float*)nullptr, 0.f));
+                            (const float*)x1f, (const uint16_t*)nullptr, y_res32, D, rstd_out,
+                            L.cfg.eps));
+  } else if (rstd_out) {
+    MB_CUDA(mb::launch_pdl(rownorm_f32_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
+                            (const float*)y_res32, (int)T, D, L.cfg.eps, rstd_out));
   }
   return MB_OK;
+}
+}  // namespace
+
+extern "C" int mb_decoder_layer_forward_ex(const void* layer, const uint16_t* x,
+                                           const float* x_res32, uint16_t* y, float* y_res32,
+                                           int B, int S, const int* start_pos, const int* kv_len,
+                                           int max_kv_len, uint16_t* k_cache, uint16_t* v_cache,
+                                           const int* block_table, int max_pages, int causal,
+                                           void* workspace, size_t workspace_bytes,
+                                           void* stream) {
+  return decoder_forward(layer, x, x_res32, y, y_res32, nullptr, nullptr, B, S, start_pos, kv_len,
+                         max_kv_len, k_cache, v_cache, block_table, max_pages, causal, workspace,
+                         workspace_bytes, stream);
+}
+
+extern "C" int mb_decoder_layer_forward_chain(const void* layer, const uint16_t* x,
+                                              const float* x_res32, const float* rstd_in,
+                                              uint16_t* y, float* y_res32, float* rstd_out, int B,
+                                              int S, const int* start_pos, const int* kv_len,
+                                              int max_kv_len, uint16_t* k_cache,
+                                              uint16_t* v_cache, const int* block_table,
+                                              int max_pages, int causal, void* workspace,
+                                              size_t workspace_bytes, void* stream) {
+  return decoder_forward(layer, x, x_res32, y, y_res32, rstd_in, rstd_out, B, S, start_pos,
+                         kv_len, max_kv_len, k_cache, v_cache, block_table, max_pages, causal,
+                         workspace, workspace_bytes, stream);
 }
 
 extern "C" int mb_decoder_layer_forward(const void* layer, const uint16_t* x, uint16_t* y, int B,

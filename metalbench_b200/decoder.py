@@ -104,7 +104,9 @@ class DecoderLayer:
                 causal: bool = True, out: torch.Tensor | None = None,
                 max_kv_len: int | None = None, kv_len: torch.Tensor | None = None,
                 x_res32: torch.Tensor | None = None,
-                y_res32: torch.Tensor | None = None) -> torch.Tensor:
+                y_res32: torch.Tensor | None = None,
+                rstd_in: torch.Tensor | None = None,
+                rstd_out: torch.Tensor | None = None) -> torch.Tensor:
         """x: [B, S, D] bf16 (or [S, D] for B = 1); start_pos: int32 [B] on the device.
 
         The new tokens' keys/values are appended at start_pos[b].. and attention
@@ -112,7 +114,10 @@ class DecoderLayer:
         the device) may be passed in when several layers share it. x_res32 /
         y_res32 (fp32, x's shape) carry the residual stream in fp32 between
         layers: x_res32 is this layer's input residual (x its bf16 rounding),
-        y_res32 receives the fp32 output."""
+        y_res32 receives the fp32 output. rstd_in / rstd_out (fp32, one entry
+        per token) chain the input RMSNorm factor between layers: rstd_out
+        receives rsqrt(mean(y_res32^2) + eps) for the next layer, which takes
+        it as rstd_in instead of computing it (rstd_out needs y_res32)."""
         squeeze = x.dim() == 2
         X = x.unsqueeze(0) if squeeze else x
         ops._cuda(X, "DecoderLayer.forward(x)", (torch.bfloat16,))
@@ -133,9 +138,18 @@ class DecoderLayer:
                 ops._cuda(t, f"DecoderLayer.forward({nm})", (torch.float32,))
                 if t.numel() != X.numel():
                     raise ValueError(f"{nm} must have x's shape")
-        _lib.call("mb_decoder_layer_forward_ex", self._h, X.data_ptr(),
-                  0 if x_res32 is None else x_res32.data_ptr(), out.data_ptr(),
-                  0 if y_res32 is None else y_res32.data_ptr(), B, S,
+        for nm, t in (("rstd_in", rstd_in), ("rstd_out", rstd_out)):
+            if t is not None:
+                ops._cuda(t, f"DecoderLayer.forward({nm})", (torch.float32,))
+                if t.numel() != B * S:
+                    raise ValueError(f"{nm} must hold one float per token")
+        if rstd_out is not None and y_res32 is None:
+            raise ValueError("rstd_out needs y_res32")
+        _lib.call("mb_decoder_layer_forward_chain", self._h, X.data_ptr(),
+                  0 if x_res32 is None else x_res32.data_ptr(),
+                  0 if rstd_in is None else rstd_in.data_ptr(), out.data_ptr(),
+                  0 if y_res32 is None else y_res32.data_ptr(),
+                  0 if rstd_out is None else rstd_out.data_ptr(), B, S,
                   start_pos.data_ptr(), kv_len.data_ptr(), max_kv_len, cache.k.data_ptr(),
                   cache.v.data_ptr(), cache.block_table.data_ptr(), cache.max_pages,
                   1 if causal else 0, ws.data_ptr(), ws_bytes, ops._stream())

@@ -86,13 +86,19 @@ class DecoderStack:
         key = tuple(x.shape)
         if getattr(self, "_res_key", None) != key:
             self._res = [torch.empty(key, dtype=torch.float32, device=x.device) for _ in range(2)]
+            # each layer hands the next its input RMSNorm factor (one per token)
+            self._rstd = [torch.empty(key[:-1], dtype=torch.float32, device=x.device)
+                          for _ in range(2)]
             self._res_key = key
-        res = None
+        res, rstd = None, None
+        last = len(self.layers) - 1
         for i, (layer, cache) in enumerate(zip(self.layers, self.caches)):
             nxt = self._res[i % 2]
+            nrstd = self._rstd[i % 2] if i < last else None
             x = layer(x, cache, start_pos, causal=causal, max_kv_len=kv_len_max,
-                      kv_len=self._kv_len, x_res32=res, y_res32=nxt)
-            res = nxt
+                      kv_len=self._kv_len, x_res32=res, y_res32=nxt, rstd_in=rstd,
+                      rstd_out=nrstd)
+            res, rstd = nxt, nrstd
         return x
 
     # ---- decode step in a CUDA graph ---------------------------------------
