@@ -1,4 +1,4 @@
-"""Multi-GPU parity (NCCL over NVLink) against the oracle, one process per GPU.
+"""Multi-GPU parity (NVLink peer-memory reduce, NCCL for set-up and prefill) against the oracle, one process per GPU.
 
 Each case runs tests/tp_worker.py MODE under torchrun with `world` processes
 and is skipped when fewer GPUs are visible. The world-1 cases run the same
